@@ -1,0 +1,389 @@
+// m4b_api.cu -- the C ABI (include/m4b.h): contract validation, dispatch and sizes.
+//
+// Validation mirrors the reference's builders + launchers (vendor/llama.cpp/ggml/src/ggml.c:
+// 3398-3540, patches/ggml-m4/m4-*.cu launchers) and supports_op (ggml-cuda.cu:5848-5885), with
+// the head geometry generalised from the Mistral-Small-4 constants to the two supported
+// geometries.  Every check runs before any CUDA call; a violation launches nothing.
+#include <algorithm>
+#include <cstring>
+
+#include "m4b_internal.h"
+
+namespace m4b {
+namespace {
+
+constexpr int kGeomBaseline = 0;
+constexpr int kGeomMistral = 1;
+
+bool type_ne(const m4b_tensor& t, int type, int64_t n0, int64_t n1, int64_t n2, int64_t n3) {
+    return t.type == type && t.ne[0] == n0 && t.ne[1] == n1 && t.ne[2] == n2 && t.ne[3] == n3;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Contiguous in dims 0..1 / 0..2 (element stride = type size, rows packed).
+bool packed3(const m4b_tensor& t, uint64_t esz) {
+    return t.nb[0] == esz && t.nb[1] == esz * static_cast<uint64_t>(t.ne[0]) &&
+           t.nb[2] == t.nb[1] * static_cast<uint64_t>(t.ne[1]);
+}
+
+// Per-device facts, cached (one process may drive several devices).
+struct DevInfo {
+    int checked = 0;
+    int ok = 0;
+    int sms = 0;
+};
+DevInfo g_dev[64];
+
+int device_check(int* sms_out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return M4B_ECUDA;
+    if (dev < 0 || dev >= 64) return M4B_EDEVICE;
+    DevInfo& d = g_dev[dev];
+    if (!d.checked) {
+        int major = 0, minor = 0, sms = 0;
+        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return M4B_ECUDA;
+        d.ok = (major == 10 && minor == 0);
+        d.sms = sms;
+        d.checked = 1;
+    }
+    if (!d.ok) return M4B_EDEVICE;
+    if (sms_out) *sms_out = d.sms;
+    return M4B_OK;
+}
+
+int n_tiles(int64_t n_kv) { return static_cast<int>((n_kv + kTileKeys - 1) / kTileKeys); }
+
+int default_splits(int64_t n_kv, int sms) {
+    const int cap = sms < kMaxSplits ? sms : kMaxSplits;
+    const int t = n_tiles(n_kv);
+    return t < cap ? t : cap;
+}
+
+int status_of(cudaError_t e) { return e == cudaSuccess ? M4B_OK : M4B_ECUDA; }
+
+// ---------------------------------------------------------------------------------------------
+// WKB
+// ---------------------------------------------------------------------------------------------
+int check_wkb(const m4b_tensor& w, const m4b_tensor& x, const m4b_tensor& dst, int* geom) {
+    if (type_ne(w, M4B_TYPE_Q8_0, 64, 256, 32, 1)) {   // m4-wkb.cu:75-81
+        *geom = kGeomMistral;
+        return M4B_ENOTSUP;
+    }
+    if (!type_ne(w, M4B_TYPE_F16, kNope, kLatent, kHeads, 1) || !packed3(w, 2)) return M4B_EINVAL;
+    if (!type_ne(x, M4B_TYPE_F32, kNope, kHeads, 1, 1) || x.nb[0] != 4 || x.nb[1] % 4 != 0 ||
+        x.nb[1] < 4u * kNope)
+        return M4B_EINVAL;
+    if (!type_ne(dst, M4B_TYPE_F32, kLatent, kHeads, 1, 1) || dst.nb[0] != 4 ||
+        dst.nb[1] % 4 != 0 || dst.nb[1] < 4u * kLatent)
+        return M4B_EINVAL;
+    if (!w.data || !x.data || !dst.data || !aligned(w.data, 16) || !aligned(x.data, 4) ||
+        !aligned(dst.data, 4))
+        return M4B_EINVAL;
+    *geom = kGeomBaseline;
+    return M4B_OK;
+}
+
+// ---------------------------------------------------------------------------------------------
+// KQKV
+// ---------------------------------------------------------------------------------------------
+int check_kqkv_inputs(const m4b_kqkv_args& a) {
+    const m4b_tensor& kc = a.src0;
+    const m4b_tensor& q = a.src1;
+    const m4b_tensor& mask = a.src2;
+    if (kc.type == M4B_TYPE_F16 && kc.ne[0] == 320) return M4B_ENOTSUP;   // Mistral K row
+    if (kc.type != M4B_TYPE_F16 || kc.ne[0] != kKRow || kc.ne[1] < 1 || kc.ne[2] != 1 ||
+        kc.ne[3] != 1 || kc.nb[0] != 2 || kc.nb[1] % 16 != 0 || kc.nb[1] < 2u * kKRow)
+        return M4B_EINVAL;
+    if (kc.ne[1] > (int64_t(1) << 30)) return M4B_EINVAL;
+    if (!type_ne(q, M4B_TYPE_F32, kKRow, kHeads, 1, 1) || q.nb[0] != 4 || q.nb[1] % 4 != 0 ||
+        q.nb[1] < 4u * kKRow)
+        return M4B_EINVAL;
+    if (mask.data != nullptr) {   // ggml_m4_kqkv: mask ne0 == n_kv, one row
+        if (mask.type != M4B_TYPE_F32 || mask.ne[0] != kc.ne[1] || mask.ne[1] != 1 ||
+            mask.ne[2] != 1 || mask.ne[3] != 1 || mask.nb[0] != 4 || !aligned(mask.data, 4))
+            return M4B_EINVAL;
+    }
+    if (!kc.data || !q.data || !aligned(kc.data, 16) || !aligned(q.data, 4)) return M4B_EINVAL;
+    if (!(a.kq_scale == a.kq_scale)) return M4B_EINVAL;   // NaN scale
+    return M4B_OK;
+}
+
+int check_kqkv(const m4b_kqkv_args& a) {
+    int rc = check_kqkv_inputs(a);
+    if (rc != M4B_OK) return rc;
+    const m4b_tensor& d = a.dst;
+    if (!type_ne(d, M4B_TYPE_F32, kLatent, 1, kHeads, 1) || d.nb[0] != 4 || d.nb[2] % 4 != 0 ||
+        d.nb[2] < 4u * kLatent || !d.data || !aligned(d.data, 4))
+        return M4B_EINVAL;
+    return M4B_OK;
+}
+
+int check_partials(const m4b_tensor& p, int64_t max_splits) {
+    if (p.type != M4B_TYPE_F32 || p.ne[0] != kPartStride || p.ne[1] != kHeads || p.ne[2] < 1 ||
+        p.ne[3] != 1 || !packed3(p, 4) || !p.data || !aligned(p.data, 16))
+        return M4B_EINVAL;
+    if (max_splits > 0 && p.ne[2] > max_splits) return M4B_EINVAL;
+    return M4B_OK;
+}
+
+KqkvLaunch make_kqkv_launch(const m4b_kqkv_args& a, int splits, float* part) {
+    KqkvLaunch l;
+    l.kcache = a.src0.data;
+    l.kcache_row_bytes = a.src0.nb[1];
+    l.n_kv = a.src0.ne[1];
+    l.q = static_cast<const float*>(a.src1.data);
+    l.q_head_stride = static_cast<int64_t>(a.src1.nb[1] / 4);
+    l.mask = static_cast<const float*>(a.src2.data);
+    l.kq_scale = a.kq_scale;
+    l.splits = splits;
+    l.part = part;
+    l.flags = a.flags;
+    return l;
+}
+
+// ---------------------------------------------------------------------------------------------
+// PHASE
+// ---------------------------------------------------------------------------------------------
+int check_wuv(const m4b_tensor& w) {
+    if (type_ne(w, M4B_TYPE_Q8_0, 256, 128, 32, 1)) return M4B_ENOTSUP;   // m4-phase.cu:212-213
+    if (!type_ne(w, M4B_TYPE_F16, kLatent, kVHead, kHeads, 1) || !packed3(w, 2) || !w.data ||
+        !aligned(w.data, 16))
+        return M4B_EINVAL;
+    return M4B_OK;
+}
+
+int check_phase_dst(const m4b_tensor& d) {
+    if (!type_ne(d, M4B_TYPE_F32, kVHead, 1, kHeads, 1) || d.nb[0] != 4 || d.nb[2] % 4 != 0 ||
+        d.nb[2] < 4u * kVHead || !d.data || !aligned(d.data, 4))
+        return M4B_EINVAL;
+    return M4B_OK;
+}
+
+int check_attn(const m4b_tensor& x) {   // F32 [512, 1, 32] with a head stride nb[2]
+    if (!type_ne(x, M4B_TYPE_F32, kLatent, 1, kHeads, 1) || x.nb[0] != 4 || x.nb[2] % 4 != 0 ||
+        x.nb[2] < 4u * kLatent || !x.data || !aligned(x.data, 4))
+        return M4B_EINVAL;
+    return M4B_OK;
+}
+
+int check_phase(const m4b_phase_args& a) {
+    const int phase = a.op_params[0];
+    switch (phase) {
+        case 0:   // KV-write: Mistral-Small-4 geometry only (m4-phase.cu:230-272)
+            return M4B_ENOTSUP;
+        case 1: {
+            int rc = check_wuv(a.src[0]);
+            if (rc != M4B_OK) return rc;
+            rc = check_attn(a.src[1]);
+            if (rc != M4B_OK) return rc;
+            return check_phase_dst(a.dst);
+        }
+        case 2: {
+            int rc = check_wuv(a.src[0]);
+            if (rc != M4B_OK) return rc;
+            rc = check_partials(a.src[1], 0);
+            if (rc != M4B_OK) return rc;
+            if (a.src[2].data != nullptr && check_attn(a.src[2]) != M4B_OK) return M4B_EINVAL;
+            return check_phase_dst(a.dst);
+        }
+        default:   // m4-phase.cu:276 GGML_ABORT("unknown phase")
+            return M4B_EINVAL;
+    }
+}
+
+}  // namespace
+}  // namespace m4b
+
+using namespace m4b;
+
+extern "C" {
+
+int m4b_abi_version(void) { return M4B_ABI_VERSION; }
+
+const char* m4b_strerror(int code) {
+    switch (code) {
+        case M4B_OK: return "ok";
+        case M4B_EINVAL: return "m4b: shape/type/stride/alignment contract violated";
+        case M4B_ESCRATCH: return "m4b: scratch missing or too small";
+        case M4B_ECUDA: return "m4b: CUDA runtime error";
+        case M4B_EDEVICE: return "m4b: current device is not sm_100";
+        case M4B_ENOTSUP: return "m4b: geometry or phase not implemented by this build";
+        case M4B_ETIMEOUT: return "m4b: a kernel's bounded wait timed out";
+        default: return "m4b: unknown status";
+    }
+}
+
+int m4b_kqkv_max_splits(void) { return kMaxSplits; }
+
+int m4b_kqkv_default_splits(int64_t n_kv) {
+    if (n_kv < 1) return 0;
+    int sms = kMaxSplits;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
+            sms = v;
+    } else {
+        cudaGetLastError();
+    }
+    return default_splits(n_kv, sms);
+}
+
+uint64_t m4b_kqkv_scratch_bytes(int geometry, int64_t n_kv) {
+    if (geometry != 0 || n_kv < 1) return 0;
+    const int s = default_splits(n_kv, kMaxSplits);
+    return static_cast<uint64_t>(s) * kHeads * kPartStride * sizeof(float);
+}
+
+uint64_t m4b_phase_scratch_bytes(int phase) {
+    return phase == 2 ? static_cast<uint64_t>(kHeads) * kLatent * sizeof(float) : 0;
+}
+
+int m4b_wkb(const m4b_wkb_args* a, m4b_stream_t stream) {
+    if (!a) return M4B_EINVAL;
+    int geom = 0;
+    int rc = check_wkb(a->src0, a->src1, a->dst, &geom);
+    if (rc != M4B_OK) return rc;
+    rc = device_check(nullptr);
+    if (rc != M4B_OK) return rc;
+    return status_of(launch_wkb_f16(a->src0.data, static_cast<const float*>(a->src1.data),
+                                    static_cast<int64_t>(a->src1.nb[1] / 4),
+                                    static_cast<float*>(a->dst.data),
+                                    static_cast<int64_t>(a->dst.nb[1] / 4), a->flags,
+                                    reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int m4b_kqkv(const m4b_kqkv_args* a, m4b_stream_t stream) {
+    if (!a) return M4B_EINVAL;
+    int rc = check_kqkv(*a);
+    if (rc != M4B_OK) return rc;
+    int sms = 0;
+    rc = device_check(&sms);
+    if (rc != M4B_OK) return rc;
+    const int64_t n_kv = a->src0.ne[1];
+    const int splits = default_splits(n_kv, sms);
+    const uint64_t need = static_cast<uint64_t>(splits) * kHeads * kPartStride * sizeof(float);
+    if (!a->scratch || a->scratch_bytes < need || !aligned(a->scratch, 16)) return M4B_ESCRATCH;
+    float* part = static_cast<float*>(a->scratch);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = launch_kqkv_partials(make_kqkv_launch(*a, splits, part), s);
+    if (e != cudaSuccess) return M4B_ECUDA;
+    e = launch_kqkv_combine(part, splits, static_cast<float*>(a->dst.data),
+                            static_cast<int64_t>(a->dst.nb[2] / 4), a->flags & M4B_FLAG_PDL, s);
+    return status_of(e);
+}
+
+int m4b_kqkv_partials(const m4b_kqkv_args* a, m4b_stream_t stream) {
+    if (!a) return M4B_EINVAL;
+    int rc = check_kqkv_inputs(*a);
+    if (rc != M4B_OK) return rc;
+    rc = check_partials(a->dst, std::min<int64_t>(kMaxSplits, n_tiles(a->src0.ne[1])));
+    if (rc != M4B_OK) return rc;
+    rc = device_check(nullptr);
+    if (rc != M4B_OK) return rc;
+    const int splits = static_cast<int>(a->dst.ne[2]);
+    return status_of(launch_kqkv_partials(
+        make_kqkv_launch(*a, splits, static_cast<float*>(a->dst.data)),
+        reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int m4b_phase(const m4b_phase_args* a, m4b_stream_t stream) {
+    if (!a) return M4B_EINVAL;
+    int rc = check_phase(*a);
+    if (rc != M4B_OK) return rc;
+    const int phase = a->op_params[0];
+    float* attn = nullptr;
+    int64_t attn_hs = kLatent;
+    if (phase == 2) {
+        if (a->src[2].data != nullptr) {
+            attn = static_cast<float*>(a->src[2].data);
+            attn_hs = static_cast<int64_t>(a->src[2].nb[2] / 4);
+        } else {
+            if (!a->scratch || a->scratch_bytes < m4b_phase_scratch_bytes(2) ||
+                !aligned(a->scratch, 16))
+                return M4B_ESCRATCH;
+            attn = static_cast<float*>(a->scratch);
+        }
+    }
+    rc = device_check(nullptr);
+    if (rc != M4B_OK) return rc;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    float* out = static_cast<float*>(a->dst.data);
+    const int64_t out_hs = static_cast<int64_t>(a->dst.nb[2] / 4);
+    if (phase == 1) {
+        return status_of(launch_wvb_f16(a->src[0].data, static_cast<const float*>(a->src[1].data),
+                                        static_cast<int64_t>(a->src[1].nb[2] / 4), out, out_hs,
+                                        a->flags, s));
+    }
+    // phase 2: merge the partial records, then W_UV (one node, two launches)
+    cudaError_t e = launch_kqkv_combine(static_cast<const float*>(a->src[1].data),
+                                        static_cast<int>(a->src[1].ne[2]), attn, attn_hs,
+                                        a->flags & M4B_FLAG_PDL, s);
+    if (e != cudaSuccess) return M4B_ECUDA;
+    return status_of(launch_wvb_f16(a->src[0].data, attn, attn_hs, out, out_hs,
+                                    a->flags & M4B_FLAG_PDL, s));
+}
+
+int m4b_supports_op(int op, const m4b_tensor* srcs, int n_srcs, const m4b_tensor* dst,
+                    const int32_t* op_params) {
+    if (!srcs || !dst) return 0;
+    switch (op) {
+        case 0: {
+            if (n_srcs < 2) return 0;
+            int geom = 0;
+            return check_wkb(srcs[0], srcs[1], *dst, &geom) == M4B_OK;
+        }
+        case 1: {
+            if (n_srcs < 2) return 0;
+            m4b_kqkv_args a;
+            std::memset(&a, 0, sizeof(a));
+            a.src0 = srcs[0];
+            a.src1 = srcs[1];
+            if (n_srcs >= 3) a.src2 = srcs[2];
+            a.dst = *dst;
+            a.kq_scale = op_params ? *reinterpret_cast<const float*>(op_params) : 1.0f;
+            return check_kqkv(a) == M4B_OK;
+        }
+        case 2: {
+            if (!op_params) return 0;
+            m4b_phase_args a;
+            std::memset(&a, 0, sizeof(a));
+            for (int i = 0; i < n_srcs && i < 6; ++i) a.src[i] = srcs[i];
+            a.dst = *dst;
+            std::memcpy(a.op_params, op_params, sizeof(int32_t) * 10);
+            return check_phase(a) == M4B_OK;
+        }
+        default:
+            return 0;
+    }
+}
+
+int m4b_resolve_flag(int flag, int gpu_core, int nt, int ragged_ok, int* enabled) {
+    if (!enabled) return M4B_EINVAL;
+    *enabled = 0;
+    if (flag < -1 || flag > 1) return M4B_EINVAL;
+    if (flag == 1 && !gpu_core) return M4B_EINVAL;                  // m1_engine.cpp:2182-2197
+    if (flag == 1 && nt > 1 && !ragged_ok) return M4B_EINVAL;       // m1_engine.cpp:2100-2110
+    const int on = (flag < 0) ? (gpu_core != 0) : (flag == 1);
+    *enabled = on && (nt == 1 || ragged_ok);                        // m1_layer.cpp:283-297
+    return M4B_OK;
+}
+
+int m4b_device_status(m4b_stream_t stream) {
+    unsigned int v = 0;
+    if (cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return M4B_ECUDA;
+    if (cudaMemcpyFromSymbol(&v, g_status, sizeof(v)) != cudaSuccess) return M4B_ECUDA;
+    if (v != 0) {
+        const unsigned int zero = 0;
+        if (cudaMemcpyToSymbol(g_status, &zero, sizeof(zero)) != cudaSuccess) return M4B_ECUDA;
+        return M4B_ETIMEOUT;
+    }
+    return M4B_OK;
+}
+
+}  // extern "C"

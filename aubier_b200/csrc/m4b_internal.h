@@ -1,0 +1,76 @@
+// m4b_internal.h -- declarations shared by the M4 kernel translation units (not part of the ABI).
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "../../include/m4b.h"
+
+namespace m4b {
+
+// BASELINE geometry (the measured one): 32 heads, q_nope 128, rope 64, latent 512, K row 576,
+// V head 128.  Reference constants for the Mistral-Small-4 geometry: engine/m1_layer.h:47-55.
+constexpr int kHeads = 32;
+constexpr int kNope = 128;
+constexpr int kRope = 64;
+constexpr int kLatent = 512;
+constexpr int kKRow = kLatent + kRope;  // 576
+constexpr int kVHead = 128;
+
+// Split-K partial record per (split, head): o[512], m (log2 units), l, 2 pad floats.
+// 516 floats = 2064 bytes keeps every record 16-byte aligned.
+constexpr int kPartStride = kLatent + 4;
+constexpr int kPartM = kLatent;
+constexpr int kPartL = kLatent + 1;
+
+constexpr int kTileKeys = 128;   // keys per KQKV tile (the tcgen05 MMA M dimension)
+constexpr int kMaxSplits = 148;  // one persistent CTA per B200 SM
+
+struct KqkvLaunch {
+    const void* kcache;
+    uint64_t kcache_row_bytes;
+    int64_t n_kv;
+    const float* q;
+    int64_t q_head_stride;  // floats
+    const float* mask;      // nullable
+    float kq_scale;
+    int splits;
+    float* part;            // [splits][kHeads][kPartStride]
+    uint32_t flags;
+};
+
+cudaError_t launch_kqkv_partials(const KqkvLaunch& a, cudaStream_t stream);
+
+// out[h][d] = merge over S partial records; out head stride in floats.
+cudaError_t launch_kqkv_combine(const float* part, int S, float* out, int64_t out_head_stride,
+                                uint32_t flags, cudaStream_t stream);
+
+// q_abs[h][r] = W_UK[h][r][:] . f16(q[h][:128]); W_UK contiguous f16 [32][512][128].
+cudaError_t launch_wkb_f16(const void* w, const float* q, int64_t q_head_stride, float* out,
+                           int64_t out_head_stride, uint32_t flags, cudaStream_t stream);
+
+// out[h][j] = W_UV[h][j][:] . f16(x[h][:512]); W_UV contiguous f16 [32][128][512].
+cudaError_t launch_wvb_f16(const void* w, const float* x, int64_t x_head_stride, float* out,
+                           int64_t out_head_stride, uint32_t flags, cudaStream_t stream);
+
+// Launch helper: plain launch, or with programmatic stream serialisation when PDL is requested.
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                   cudaStream_t stream, uint32_t flags, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (flags & M4B_FLAG_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+}  // namespace m4b

@@ -1,0 +1,513 @@
+// m4b_kqkv.cu -- GGML_OP_M4_KQKV on sm_100a: split-K online-softmax MLA decode attention with
+// TMA-staged KV tiles and both contractions on tcgen05 tensor cores, accumulators in TMEM.
+//
+// What the op computes (the reference's contract, patches/ggml-m4/m4-kqkv.cu:1-37 and the
+// unfused graph it replaces, engine/m1_layer.cpp:478-494):
+//   s[h][n]  = (K[n] . q[h]) * kq_scale + mask[n]          K[n] = kcache row n, 576 f16
+//   out[h]   = sum_n softmax_n(s[h][.]) * V[n]             V[n] = kcache row n, first 512 f16
+// All 32 heads share every KV row (MLA's latent cache), so per tile of 128 keys the work is two
+// dense products with the heads as the narrow dimension:
+//   MMA1  S^T[128 keys x 32 heads]   = Ktile[128 x 576] . Q^T[576 x 32]     (K-major A and B)
+//   MMA2  O^T[512 lat  x 32 heads]  += Vtile^T[512 x 128] . P[128 x 32]     (A read MN-major)
+// V is the first 512 columns of the SAME shared-memory tile MMA1 consumed, read through an
+// MN-major descriptor, so every KV byte crosses HBM exactly once.
+//
+// CTA = one split (a contiguous run of tiles, balanced as in m4-kqkv.cu:204-218), persistent,
+// one per SM.  Warp roles (320 threads):
+//   warp 0      TMA producer: per tile, the rope chunk (cols 512..575) then four 128-column
+//               "pairs" of the latent, into a 5-slot pair ring + 1 rope slot (smem 176 KB)
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2..9  softmax: two groups of four warps, group g owns heads 16g..16g+15; warp w reads
+//               TMEM lanes 32*(w%4).. (one key per thread), does the online softmax in log2 units
+//               with a lazy rescale of O (only when a head's max grows by more than 2^8), writes
+//               P (f16) for MMA2, and writes the split's (o, m, l) partial at the end.
+// Numerics: q and P are rounded to f16 for the tensor cores -- the same rounding points as the
+// reference CPU graph, whose mul_mat converts an F32 src1 to F16 (ggml-cpu.c:1330-1375) -- and
+// both products accumulate in f32.
+#include <cstddef>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include "m4b_internal.h"
+#include "m4b_ptx.cuh"
+
+namespace m4b {
+namespace kq {
+
+constexpr int H = kHeads;
+constexpr int D = kKRow;               // 576
+constexpr int TK = kTileKeys;          // 128 keys per tile
+constexpr int CHUNK_BYTES = TK * 128;  // 128 keys x 64 f16 columns = 16 KB (one SW128 atom column)
+constexpr int PAIR_BYTES = 2 * CHUNK_BYTES;
+constexpr int NPAIR = 5;               // latent ring: 5 x 32 KB
+constexpr int QCH_BYTES = H * 128;     // 32 heads x 64 columns f16 = 4 KB
+constexpr int NQCH = D / 64;           // 9
+constexpr int P_BYTES = 2 * QCH_BYTES; // 32 heads x 128 keys f16
+
+constexpr int OFF_PAIR = 0;
+constexpr int OFF_ROPE = OFF_PAIR + NPAIR * PAIR_BYTES;
+constexpr int OFF_Q = OFF_ROPE + CHUNK_BYTES;
+constexpr int OFF_P = OFF_Q + NQCH * QCH_BYTES;
+constexpr int OFF_CTRL = OFF_P + P_BYTES;
+constexpr int CTRL_BYTES = 2048;
+constexpr int SMEM_BYTES = OFF_CTRL + CTRL_BYTES + 1024;  // + slack to align the base to 1 KB
+
+constexpr int NTHREADS = 320;
+constexpr int TMEM_COLS = 256;   // S^T: cols [0,32); O^T: cols [32,160) as 4 blocks of 32
+constexpr int TM_S = 0;
+constexpr int TM_O = 32;
+constexpr float RESCALE_THRESH = 8.0f;  // log2 units: P stays <= 2^8 between rescales
+constexpr float LOG2E = 1.4426950408889634f;
+
+struct Ctrl {
+    uint64_t pair_full[NPAIR];
+    uint64_t pair_empty[NPAIR];
+    uint64_t rope_full, rope_empty;
+    uint64_t q_full, s_full, p_full, o_full;
+    uint64_t red_full[2];   // per head group: the 4 warps' tile maxima are in red[]
+    uint64_t redl_full[2];  // per head group: the 4 warps' row sums are in red_l[]
+    uint32_t tmem_base;
+    int abort_flag;
+    alignas(16) float red[2][2][4][16];  // [tile parity][group][quadrant][head], read as float4
+    alignas(16) float red_l[2][4][16];   // [group][quadrant][head]
+};
+static_assert(sizeof(Ctrl) <= CTRL_BYTES, "control block too large");
+static_assert(offsetof(Ctrl, red) % 16 == 0 && offsetof(Ctrl, red_l) % 16 == 0,
+              "reduction buffers are read with 16-byte vector loads");
+static_assert(OFF_CTRL % 16 == 0 && OFF_Q % 1024 == 0 && OFF_P % 1024 == 0 && OFF_ROPE % 1024 == 0,
+              "TMA / UMMA operands need 1 KB alignment, vector accesses 16 B");
+static_assert(SMEM_BYTES <= 232448, "exceeds the 227 KB per-CTA shared memory of sm_100");
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// A wait whose result is the same in every lane of the warp (the softmax warps run
+// warp-collective tcgen05.ld/st and shuffles, which need a converged warp).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    const bool ok = mbar_wait(bar, parity, abort_flag);
+    return __all_sync(0xffffffffu, ok);
+}
+
+// Column max / sum of a 32(lanes) x 16(values) block held one row per lane: after the
+// butterfly each lane holds the reduction of value index (lane >> 1) (lanes 2j, 2j+1 agree).
+template <bool kMax>
+__device__ __forceinline__ float transpose_reduce16(const float (&in)[16], int lane) {
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = in[j];
+#pragma unroll
+    for (int n = 16, off = 16; n > 1; n >>= 1, off >>= 1) {
+        const bool upper = (lane & off) != 0;
+        const int half = n >> 1;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float send = upper ? v[i] : v[i + half];
+            const float keep = upper ? v[i + half] : v[i];
+            const float recv = __shfl_xor_sync(0xffffffffu, send, off);
+            v[i] = kMax ? fmaxf(keep, recv) : keep + recv;
+        }
+    }
+    const float r = __shfl_xor_sync(0xffffffffu, v[0], 1);
+    return kMax ? fmaxf(v[0], r) : v[0] + r;
+}
+
+__global__ void __launch_bounds__(NTHREADS, 1)
+kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __restrict__ q,
+                    int64_t q_hs, const float* __restrict__ mask, float kq_scale, int n_kv,
+                    int splits, float* __restrict__ part, uint32_t flags) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    Ctrl& C = *reinterpret_cast<Ctrl*>(smem + OFF_CTRL);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int split = blockIdx.x;
+
+    const int n_tiles = (n_kv + TK - 1) / TK;
+    const int base_t = n_tiles / splits;
+    const int rem = n_tiles % splits;
+    const int t0 = split * base_t + min(split, rem);
+    const int nt = base_t + (split < rem ? 1 : 0);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NPAIR; ++i) {
+            mbar_init(&C.pair_full[i], 1);
+            mbar_init(&C.pair_empty[i], 1);
+        }
+        mbar_init(&C.rope_full, 1);
+        mbar_init(&C.rope_empty, 1);
+        mbar_init(&C.q_full, 256);
+        mbar_init(&C.s_full, 1);
+        mbar_init(&C.p_full, 8);
+        mbar_init(&C.o_full, 1);
+        for (int g = 0; g < 2; ++g) {
+            mbar_init(&C.red_full[g], 4);
+            mbar_init(&C.redl_full[g], 4);
+        }
+        C.abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) tma_prefetch_desc(&tmap);
+    if (warp == 1) {
+        tmem_alloc(&C.tmem_base, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = C.tmem_base;
+    volatile int* abort_flag = &C.abort_flag;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            if (!(flags & M4B_FLAG_KV_STATIC)) pdl_wait();
+            const uint64_t pol = l2_policy_evict_first();
+            bool ok = true;
+            int rope_issued = 0, pair_issued = 0;
+            for (int i = 0; i < nt && ok; ++i) {
+                const int key0 = (t0 + i) * TK;
+                ok = mbar_wait(&C.rope_empty, (i & 1) ^ 1, abort_flag);
+                if (!ok) break;
+                mbar_arrive_expect_tx(&C.rope_full, CHUNK_BYTES);
+                tma_load_2d(smem + OFF_ROPE, &tmap, kLatent, key0, &C.rope_full, pol);
+                ++rope_issued;
+                for (int p = 0; p < 4 && ok; ++p) {
+                    const int g = 4 * i + p;
+                    const int slot = g % NPAIR;
+                    ok = mbar_wait(&C.pair_empty[slot], ((g / NPAIR) & 1) ^ 1, abort_flag);
+                    if (!ok) break;
+                    mbar_arrive_expect_tx(&C.pair_full[slot], PAIR_BYTES);
+                    uint8_t* dst = smem + OFF_PAIR + slot * PAIR_BYTES;
+                    tma_load_2d(dst, &tmap, 128 * p, key0, &C.pair_full[slot], pol);
+                    tma_load_2d(dst + CHUNK_BYTES, &tmap, 128 * p + 64, key0, &C.pair_full[slot], pol);
+                    ++pair_issued;
+                }
+            }
+            if (*abort_flag) {
+                // let this CTA's own copies land before its shared memory is released
+                if (rope_issued > 0) mbar_drain(&C.rope_full, (rope_issued - 1) & 1);
+                for (int slot = 0; slot < NPAIR; ++slot) {
+                    const int n = pair_issued > slot ? (pair_issued - slot + NPAIR - 1) / NPAIR : 0;
+                    if (n > 0) mbar_drain(&C.pair_full[slot], (n - 1) & 1);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = idesc_f16_f32(128, 32, false, false);
+            constexpr uint32_t idesc_o = idesc_f16_f32(128, 32, true, false);
+            const uint32_t q_base = smem_u32(smem + OFF_Q);
+            const uint32_t p_base = smem_u32(smem + OFF_P);
+            const uint32_t rope_base = smem_u32(smem + OFF_ROPE);
+            const uint32_t pair_base = smem_u32(smem + OFF_PAIR);
+            const uint32_t tS = tmem + TM_S;
+            const uint32_t tO = tmem + TM_O;
+            bool ok = mbar_wait(&C.q_full, 0, abort_flag);
+            for (int i = 0; i < nt && ok; ++i) {
+                // MMA1: S^T = Ktile . Q^T over the 9 column chunks (rope chunk first)
+                ok = mbar_wait(&C.rope_full, i & 1, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_f16(tS, sdesc_sw128(rope_base + kk * 32, 16, 1024),
+                            sdesc_sw128(q_base + 8 * QCH_BYTES + kk * 32, 16, 1024), idesc_s,
+                            kk > 0 ? 1u : 0u);
+                mma_commit(&C.rope_empty);
+                for (int p = 0; p < 4 && ok; ++p) {
+                    const int g = 4 * i + p;
+                    const int slot = g % NPAIR;
+                    ok = mbar_wait(&C.pair_full[slot], (g / NPAIR) & 1, abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t pb = pair_base + slot * PAIR_BYTES;
+#pragma unroll
+                    for (int hf = 0; hf < 2; ++hf) {
+                        const int c = 2 * p + hf;
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            mma_f16(tS, sdesc_sw128(pb + hf * CHUNK_BYTES + kk * 32, 16, 1024),
+                                    sdesc_sw128(q_base + c * QCH_BYTES + kk * 32, 16, 1024),
+                                    idesc_s, 1u);
+                    }
+                }
+                if (!ok) break;
+                mma_commit(&C.s_full);
+                // MMA2: O^T[128-latent block b] += Vtile^T . P, V read MN-major from the pair
+                ok = mbar_wait(&C.p_full, i & 1, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                for (int b = 0; b < 4; ++b) {
+                    const int g = 4 * i + b;
+                    const int slot = g % NPAIR;
+                    const uint32_t pb = pair_base + slot * PAIR_BYTES;
+#pragma unroll
+                    for (int ks = 0; ks < 8; ++ks)
+                        mma_f16(tO + 32 * b, sdesc_sw128(pb + ks * 2048, CHUNK_BYTES, 1024),
+                                sdesc_sw128(p_base + (ks >> 2) * QCH_BYTES + (ks & 3) * 32, 16, 1024),
+                                idesc_o, (i > 0 || ks > 0) ? 1u : 0u);
+                    mma_commit(&C.pair_empty[slot]);
+                }
+            }
+            mma_commit(&C.o_full);
+        }
+    } else {
+        // ------------------------------------------------------------------ softmax warps
+        const int sw = warp - 2;       // 0..7
+        const int grp = sw >> 2;       // heads 16*grp .. 16*grp+15
+        const int quad = warp & 3;     // TMEM lane quadrant this warp may access
+        const int key_in_tile = quad * 32 + lane;
+        const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+
+        // Stage Q (f32 -> f16, round to nearest even) into the K-major SW128 layout.
+        pdl_wait();
+        for (int u = threadIdx.x - 64; u < H * (D / 8); u += 256) {
+            const int h = u / (D / 8);
+            const int col = (u % (D / 8)) * 8;
+            const float* src = q + h * q_hs + col;
+            uint4 pk;
+            pk.x = pack_half2(src[0], src[1]);
+            pk.y = pack_half2(src[2], src[3]);
+            pk.z = pack_half2(src[4], src[5]);
+            pk.w = pack_half2(src[6], src[7]);
+            const int chunk = col >> 6;
+            const int unit = (col & 63) >> 3;
+            *reinterpret_cast<uint4*>(smem + OFF_Q + chunk * QCH_BYTES + h * 128 +
+                                      ((unit ^ (h & 7)) << 4)) = pk;
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&C.q_full);
+
+        // P destination of this thread's key (column key_in_tile of 32 head rows)
+        const int pchunk = key_in_tile >> 6;
+        const int pkk = key_in_tile & 63;
+        uint8_t* const prow0 = smem + OFF_P + pchunk * QCH_BYTES + (pkk & 7) * 2;
+        const int punit = pkk >> 3;
+
+        float m_run[16], l_part[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            m_run[j] = -INFINITY;
+            l_part[j] = 0.0f;
+        }
+        bool ok = true;
+        for (int i = 0; i < nt; ++i) {
+            const int kg = (t0 + i) * TK + key_in_tile;
+            const bool valid = kg < n_kv;
+            float mv = 0.0f;
+            if (valid && mask != nullptr) mv = __ldg(mask + kg);
+            ok = warp_wait(&C.s_full, i & 1, abort_flag);
+            if (!ok) break;
+            tc_fence_after();
+            float s[16];
+            tmem_ld16(tmem + lane_off + TM_S + 16 * grp, s);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                float t = s[j] * kq_scale;   // soft_max_ext: scale, then add the mask
+                t = t + mv;
+                s[j] = valid ? t * LOG2E : -INFINITY;
+            }
+            const float wmax = transpose_reduce16<true>(s, lane);
+            if ((lane & 1) == 0) C.red[i & 1][grp][quad][lane >> 1] = wmax;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&C.red_full[grp]);
+            ok = warp_wait(&C.red_full[grp], i & 1, abort_flag);
+            if (!ok) break;
+            float tmax[16];
+#pragma unroll
+            for (int j4 = 0; j4 < 4; ++j4) {
+                float4 a = *reinterpret_cast<const float4*>(&C.red[i & 1][grp][0][4 * j4]);
+#pragma unroll
+                for (int qd = 1; qd < 4; ++qd) {
+                    const float4 b = *reinterpret_cast<const float4*>(&C.red[i & 1][grp][qd][4 * j4]);
+                    a.x = fmaxf(a.x, b.x);
+                    a.y = fmaxf(a.y, b.y);
+                    a.z = fmaxf(a.z, b.z);
+                    a.w = fmaxf(a.w, b.w);
+                }
+                tmax[4 * j4 + 0] = a.x;
+                tmax[4 * j4 + 1] = a.y;
+                tmax[4 * j4 + 2] = a.z;
+                tmax[4 * j4 + 3] = a.w;
+            }
+            // Lazy rescale: keep the running max unless a head's max grows by > 2^8.
+            bool need = false;
+            float alpha[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                alpha[j] = 1.0f;
+                const float mn = fmaxf(m_run[j], tmax[j]);
+                if (m_run[j] == -INFINITY) {
+                    m_run[j] = mn;          // nothing accumulated yet for this head
+                } else if (mn - m_run[j] > RESCALE_THRESH) {
+                    alpha[j] = exp2f(m_run[j] - mn);
+                    m_run[j] = mn;
+                    need = true;
+                }
+            }
+            if (need) {   // uniform across the group: every thread computed the same maxima
+#pragma unroll
+                for (int j = 0; j < 16; ++j) l_part[j] *= alpha[j];
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    float o[16];
+                    const uint32_t ta = tmem + lane_off + TM_O + 32 * b + 16 * grp;
+                    tmem_ld16(ta, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) o[j] *= alpha[j];
+                    tmem_st16(ta, o);
+                }
+                tmem_wait_st();
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const float p = (s[j] == -INFINITY) ? 0.0f : exp2f(s[j] - m_run[j]);
+                l_part[j] += p;
+                const int h = 16 * grp + j;
+                *reinterpret_cast<__half*>(prow0 + h * 128 + ((punit ^ (h & 7)) << 4)) =
+                    __float2half_rn(p);
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&C.p_full);
+        }
+
+        // ---- epilogue: the split's partial record (o[512], m, l) per head
+        float* prec = part + static_cast<size_t>(split) * H * kPartStride;
+        const float lsum = transpose_reduce16<false>(l_part, lane);
+        if (ok) {
+            if ((lane & 1) == 0) C.red_l[grp][quad][lane >> 1] = lsum;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&C.redl_full[grp]);
+            ok = warp_wait(&C.redl_full[grp], 0, abort_flag);
+        }
+        if (ok && quad == 0 && lane < 16) {
+            const int h = 16 * grp + lane;
+            const float l = C.red_l[grp][0][lane] + C.red_l[grp][1][lane] +
+                            C.red_l[grp][2][lane] + C.red_l[grp][3][lane];
+            float m = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (lane == j) m = m_run[j];
+            prec[h * kPartStride + kPartM] = m;
+            prec[h * kPartStride + kPartL] = l;
+        }
+        if (warp_wait(&C.o_full, 0, abort_flag) && ok) {
+            tc_fence_after();
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                float o[16];
+                tmem_ld16(tmem + lane_off + TM_O + 32 * b + 16 * grp, o);
+                tmem_wait_ld();
+                const int d = 128 * b + quad * 32 + lane;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) prec[(16 * grp + j) * kPartStride + d] = o[j];
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// Merge S partial records per head (m4-kqkv.cu:318-338 rule, log2 units); one thread per
+// output element, grid (heads, latent / 128).
+__global__ void __launch_bounds__(128)
+kqkv_combine_kernel(const float* __restrict__ part, int S, float* __restrict__ out, int64_t out_hs) {
+    pdl_wait();
+    const int h = blockIdx.x;
+    const int d = blockIdx.y * 128 + threadIdx.x;
+    const float* ph = part + static_cast<size_t>(h) * kPartStride;
+    const size_t ss = static_cast<size_t>(H) * kPartStride;
+    float mstar = -INFINITY;
+    for (int s = 0; s < S; ++s) mstar = fmaxf(mstar, __ldg(ph + s * ss + kPartM));
+    float l = 0.0f, o = 0.0f;
+    if (mstar > -INFINITY) {
+        int s = 0;
+        for (; s + 4 <= S; s += 4) {
+            float m4[4], l4[4], o4[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                m4[u] = __ldg(ph + (s + u) * ss + kPartM);
+                l4[u] = __ldg(ph + (s + u) * ss + kPartL);
+                o4[u] = __ldg(ph + (s + u) * ss + d);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (m4[u] > -INFINITY) {
+                    const float a = exp2f(m4[u] - mstar);
+                    l += l4[u] * a;
+                    o += o4[u] * a;
+                }
+            }
+        }
+        for (; s < S; ++s) {
+            const float m = __ldg(ph + s * ss + kPartM);
+            if (m > -INFINITY) {
+                const float a = exp2f(m - mstar);
+                l += __ldg(ph + s * ss + kPartL) * a;
+                o += __ldg(ph + s * ss + d) * a;
+            }
+        }
+    }
+    out[h * out_hs + d] = (mstar > -INFINITY) ? o / l : 0.0f;
+}
+
+}  // namespace kq
+
+cudaError_t launch_kqkv_partials(const KqkvLaunch& a, cudaStream_t stream) {
+    using namespace kq;
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (encode == nullptr) {
+        cudaDriverEntryPointQueryResult qres;
+        void* fn = nullptr;
+        cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
+                                                         cudaEnableDefault, &qres);
+        if (e != cudaSuccess || qres != cudaDriverEntryPointSuccess || fn == nullptr)
+            return e != cudaSuccess ? e : cudaErrorNotSupported;
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    CUtensorMap tmap;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kKRow), static_cast<cuuint64_t>(a.n_kv)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.kcache_row_bytes)};
+    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(TK)};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.kcache),
+                        dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+
+    static uint64_t attr_set = 0;   // one bit per device ordinal
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 64 || !((attr_set >> dev) & 1)) {
+        e = cudaFuncSetAttribute(kqkv_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) attr_set |= 1ull << dev;
+    }
+    return launch(kqkv_partial_kernel, dim3(a.splits), dim3(NTHREADS), SMEM_BYTES, stream, a.flags,
+                  tmap, a.q, a.q_head_stride, a.mask, a.kq_scale, static_cast<int>(a.n_kv),
+                  a.splits, a.part, a.flags);
+}
+
+cudaError_t launch_kqkv_combine(const float* part, int S, float* out, int64_t out_hs,
+                                uint32_t flags, cudaStream_t stream) {
+    return launch(kq::kqkv_combine_kernel, dim3(kHeads, kLatent / 128), dim3(128), 0, stream, flags,
+                  part, S, out, out_hs);
+}
+
+}  // namespace m4b

@@ -1,0 +1,197 @@
+/*
+ * m4b.h -- C ABI of the B200 (sm_100a) implementation of aubier's fused MLA decode-attention ops.
+ *
+ * The reference (jmars/aubier) exposes the path as three ggml custom ops, dispatched by the
+ * patched ggml-cuda backend (patches/ggml-m4/custom-op-m4.patch, ggml-cuda.cu:2504-2512):
+ *
+ *   GGML_OP_M4_WKB    ggml_cuda_m4_wkb(ctx, dst)    patches/ggml-m4/m4-wkb.cu:71-86
+ *   GGML_OP_M4_KQKV   ggml_cuda_m4_kqkv(ctx, dst)   patches/ggml-m4/m4-kqkv.cu:340-378
+ *   GGML_OP_M4_PHASE  ggml_cuda_m4_phase(ctx, dst)  patches/ggml-m4/m4-phase.cu:205-277
+ *
+ * Each entry point below replaces the body of one of those launchers: a ggml-cuda shim copies
+ * dst->src[i] (data, type, ne[], nb[]), dst and dst->op_params into the POD argument struct and
+ * calls the entry point on ctx.stream(); a nonzero return becomes GGML_ABORT, the reference's
+ * assert-on-contract behaviour.  Plain pointers and sizes only: no ggml, torch or CUDA types.
+ *
+ * Contract shared by every launch entry point (the reference's, patches/README.md:16-18):
+ *   - one stream, plain kernel launches, no host synchronisation and no allocation, so a call is
+ *     legal inside CUDA-graph capture; scratch memory is passed in by the caller;
+ *   - device pointers only; a host pointer is a caller bug (the reference's ops have no CPU path:
+ *     ggml-cpu.c:2064-2082 aborts);
+ *   - shapes, types and strides are validated before any launch; a violation returns
+ *     M4B_EINVAL and launches nothing (the reference's GGML_ASSERTs, e.g. m4-kqkv.cu:345-355).
+ *
+ * Geometries (engine/m1_layer.h:47-55 and the BASELINE shape; selected from the tensors' shapes,
+ * never from a flag):
+ *   BASELINE      32 heads, q_nope 128, rope 64, latent 512, K row 576, V head 128, f16 W_UK/W_UV
+ *   MISTRAL_SMALL 32 heads, q_nope 64,  rope 64, latent 256, K row 320, V head 128, Q8_0 W_UK/W_UV
+ *
+ * Tensor layouts use ggml conventions: ne[0] is the innermost (contiguous) dimension, nb[] are
+ * byte strides, types are ggml_type ids.
+ */
+#ifndef M4B_H
+#define M4B_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define M4B_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define M4B_API __attribute__((visibility("default")))
+#else
+#define M4B_API
+#endif
+
+/* The stream argument is a cudaStream_t (NULL = legacy default stream). */
+typedef struct CUstream_st * m4b_stream_t;
+
+/* Return codes. */
+enum m4b_status {
+    M4B_OK       = 0,
+    M4B_EINVAL   = 1, /* shape / type / stride / alignment contract violated: nothing launched */
+    M4B_ESCRATCH = 2, /* scratch missing or smaller than the m4b_*_scratch_bytes() requirement */
+    M4B_ECUDA    = 3, /* a CUDA runtime call or launch failed */
+    M4B_EDEVICE  = 4, /* the current device is not an sm_100 part */
+    M4B_ENOTSUP  = 5, /* valid ggml op, but a geometry / phase this build does not implement */
+    M4B_ETIMEOUT = 6  /* reported by m4b_device_status(): a kernel's bounded wait gave up */
+};
+
+/* ggml_type ids (vendor/llama.cpp/ggml/include/ggml.h) of the types these ops accept. */
+enum m4b_type {
+    M4B_TYPE_F32  = 0,
+    M4B_TYPE_F16  = 1,
+    M4B_TYPE_Q8_0 = 8,
+    M4B_TYPE_I32  = 26,
+    M4B_TYPE_I64  = 27
+};
+
+/* One operand: the fields of ggml_tensor the kernels read. */
+typedef struct m4b_tensor {
+    void *   data;   /* device pointer; NULL marks an absent optional operand */
+    int32_t  type;   /* enum m4b_type */
+    int32_t  _pad;
+    int64_t  ne[4];  /* elements per dimension, ne[0] innermost */
+    uint64_t nb[4];  /* byte strides */
+} m4b_tensor;
+
+/* Launch flags (all optional). */
+enum m4b_flags {
+    /* launch with programmatic stream serialisation: the kernel may start while the previous
+       kernel on the stream drains and waits (griddepcontrol.wait) before touching its inputs */
+    M4B_FLAG_PDL       = 1u << 0,
+    /* with M4B_FLAG_PDL: the KV cache is not written by the kernels immediately before this one,
+       so KQKV may start streaming it before the preceding kernel finishes */
+    M4B_FLAG_KV_STATIC = 1u << 1
+};
+
+/*
+ * GGML_OP_M4_WKB -- the MLA absorption gemv, q_abs[h] = W_UK[h] . q_nope[h].
+ * Replaces ggml_cuda_m4_wkb (patches/ggml-m4/m4-wkb.cu:71-86); builder ggml_m4_wkb
+ * (vendor/llama.cpp/ggml/src/ggml.c:3398-3423).
+ *   src0  W_UK    F16 [128, 512, 32]  (BASELINE)   |  Q8_0 [64, 256, 32]  (MISTRAL_SMALL)
+ *   src1  q_nope  F32 [128, 32, 1]    any head stride nb[1] (the engine's view has 768 / 512 B)
+ *   dst   q_abs   F32 [512, 32, 1]    any head stride nb[1] >= 4*ne[0] (may point into Qcur)
+ */
+typedef struct m4b_wkb_args {
+    m4b_tensor src0, src1, dst;
+    uint32_t   flags;
+} m4b_wkb_args;
+
+M4B_API int m4b_wkb(const m4b_wkb_args * args, m4b_stream_t stream);
+
+/*
+ * GGML_OP_M4_KQKV -- fused scores + masked softmax + V contraction over the shared latent KV cache.
+ * Replaces ggml_cuda_m4_kqkv (patches/ggml-m4/m4-kqkv.cu:340-378); builder ggml_m4_kqkv
+ * (ggml.c:3425-3459).  op_params[0] = kq_scale.
+ *   src0  kcache  F16 [576, N, 1, 1]   N >= 1 dynamic; nb[1] multiple of 16; V = rows [0, 512)
+ *   src1  q       F32 [576, 32, 1, 1]  head stride nb[1]
+ *   src2  mask    F32 [N, 1, 1, 1]     0 / -INF (optional here: data == NULL means all zero)
+ *   dst   out     F32 [512, 1, 32, 1]  head stride nb[2]; a fully masked head yields 0
+ * Needs scratch >= m4b_kqkv_scratch_bytes(geometry, N) (split-K partials; the reference keeps
+ * them in a static device array, m4-kqkv.cu:52-72).
+ */
+typedef struct m4b_kqkv_args {
+    m4b_tensor src0, src1, src2, dst;
+    float      kq_scale;
+    uint32_t   flags;
+    void *     scratch;
+    uint64_t   scratch_bytes;
+} m4b_kqkv_args;
+
+M4B_API int m4b_kqkv(const m4b_kqkv_args * args, m4b_stream_t stream);
+
+/*
+ * KQKV, split-K partials only (no reference counterpart: the additive op the multi-GPU and fused
+ * paths use; the partial is the (m, l, o) record of m4-kqkv.cu:306-311).
+ *   dst  partials F32 [516, 32, S, 1] contiguous: per (split, head) o[512] then m (log2 units),
+ *        l, 2 pad floats.  1 <= S <= min(m4b_kqkv_max_splits(), ceil(N / 128)).
+ * src0..src2 and kq_scale as for m4b_kqkv; scratch unused.
+ */
+M4B_API int m4b_kqkv_partials(const m4b_kqkv_args * args, m4b_stream_t stream);
+
+/*
+ * GGML_OP_M4_PHASE -- the remaining per-token phases, selected by op_params[0].
+ * Replaces ggml_cuda_m4_phase (patches/ggml-m4/m4-phase.cu:205-277); builders
+ * ggml_m4_phase_kvwrite / ggml_m4_phase_wvb (ggml.c:3461-3539).
+ *   phase 0  KV-write   (MISTRAL_SMALL geometry)                          -> M4B_ENOTSUP here
+ *   phase 1  WVB        src0 W_UV F16 [512, 128, 32]; src1 x F32 [512, 1, 32] (nb[2] head
+ *                       stride); dst F32 [128, 1, 32]
+ *   phase 2  COMBINE_WVB (additive selector): src0 W_UV F16 [512, 128, 32]; src1 partials
+ *                       F32 [516, 32, S] (m4b_kqkv_partials layout, any S >= 1, e.g. gathered
+ *                       from several GPUs); dst F32 [128, 1, 32]; optional src2 F32
+ *                       [512, 1, 32] receives the merged attention output.  Needs scratch
+ *                       >= m4b_phase_scratch_bytes(2) unless src2 is given.
+ * op_params follow ggml.c:3464-3468 (an int32 array): [0] phase, [1..6] rope f32, [7] eps,
+ * [8] n_dims, [9] n_ctx_orig.
+ */
+typedef struct m4b_phase_args {
+    m4b_tensor src[6];
+    m4b_tensor dst;
+    int32_t    op_params[16];
+    uint32_t   flags;
+    void *     scratch;
+    uint64_t   scratch_bytes;
+} m4b_phase_args;
+
+M4B_API int m4b_phase(const m4b_phase_args * args, m4b_stream_t stream);
+
+/* Sizes.  geometry: 0 = BASELINE, 1 = MISTRAL_SMALL. */
+M4B_API uint64_t m4b_kqkv_scratch_bytes(int geometry, int64_t n_kv);
+M4B_API uint64_t m4b_phase_scratch_bytes(int phase);
+M4B_API int      m4b_kqkv_default_splits(int64_t n_kv); /* the split count m4b_kqkv uses */
+M4B_API int      m4b_kqkv_max_splits(void);
+
+/*
+ * The reference's supports_op (ggml-cuda.cu:5848-5885) for the three ops: 1 when the shapes and
+ * types match a supported geometry (no launch, no CUDA call), 0 otherwise.  op: 0 = WKB,
+ * 1 = KQKV, 2 = PHASE (phase from op_params[0]).  srcs: up to 6 operands, dst: the output.
+ */
+M4B_API int m4b_supports_op(int op, const m4b_tensor * srcs, int n_srcs, const m4b_tensor * dst,
+                    const int32_t * op_params);
+
+/*
+ * The tri-state enable flag of the engine (LoopArgs::m4_*, engine/m1_session.h:152-166, resolved
+ * in engine/m1_engine.cpp:2170-2197 and gated in engine/m1_layer.cpp:283-297):
+ * flag -1 = AUTO (on iff gpu_core), 0 = off (stock ops), 1 = explicit on (needs gpu_core).
+ * Writes the resolved on/off to *enabled (on also requires nt == 1 unless the op supports the
+ * ragged extension) and returns M4B_OK, or M4B_EINVAL for explicit 1 without gpu_core or a flag
+ * outside {-1, 0, 1}.
+ */
+M4B_API int m4b_resolve_flag(int flag, int gpu_core, int nt, int ragged_ok, int * enabled);
+
+/* Reads and clears the device status word (M4B_OK or M4B_ETIMEOUT); synchronises the stream. */
+M4B_API int m4b_device_status(m4b_stream_t stream);
+
+M4B_API const char * m4b_strerror(int code);
+M4B_API int          m4b_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* M4B_H */

@@ -1,0 +1,92 @@
+"""Seeded synthetic inputs for the MLA decode-attention parity tests.
+
+A self-contained generator (splitmix64 -> 53-bit uniforms -> Box-Muller normals) so the committed
+golden fixtures do not depend on any library's random stream.  Distributions follow the
+reference's config 1 (BASELINE config): W_UK, W_UV ~ N(0, 0.02) stored as f16; q and the KV cache
+~ N(0, 1), q in f32 and the cache in f16; softmax scale 1/sqrt(nope + rope).
+
+Geometry names follow the reference (engine/m1_layer.h:47-55): H heads, nope, rope, R = latent
+(kv_lora_rank), D = R + rope (the KV row), V = value head width.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+
+_M64 = np.uint64(0xFFFFFFFFFFFFFFFF)
+
+
+def _splitmix64(seed: int, n: int) -> np.ndarray:
+    with np.errstate(over="ignore"):
+        idx = np.arange(1, n + 1, dtype=np.uint64)
+        z = np.uint64(seed & 0xFFFFFFFFFFFFFFFF) + idx * np.uint64(0x9E3779B97F4A7C15)
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        z = z ^ (z >> np.uint64(31))
+    return z
+
+
+def normal(seed: int, n: int) -> np.ndarray:
+    """n standard normals (float64) from a seed, bit-stable across numpy versions."""
+    m = (n + 1) // 2
+    u = _splitmix64(seed, 2 * m)
+    u1 = ((u[0::2] >> np.uint64(11)).astype(np.float64) + 1.0) * (1.0 / 9007199254740993.0)
+    u2 = (u[1::2] >> np.uint64(11)).astype(np.float64) * (1.0 / 9007199254740992.0)
+    r = np.sqrt(-2.0 * np.log(u1))
+    z = np.empty(2 * m, np.float64)
+    z[0::2] = r * np.cos(2.0 * math.pi * u2)
+    z[1::2] = r * np.sin(2.0 * math.pi * u2)
+    return z[:n]
+
+
+def uniform_int(seed: int, n: int, lo: int, hi: int) -> np.ndarray:
+    """n integers uniform on [lo, hi] (inclusive)."""
+    u = _splitmix64(seed, n)
+    return (lo + (u % np.uint64(hi - lo + 1)).astype(np.int64)).astype(np.int64)
+
+
+@dataclass(frozen=True)
+class Geometry:
+    H: int = 32
+    nope: int = 128
+    rope: int = 64
+    R: int = 512
+    V: int = 128
+
+    @property
+    def D(self) -> int:
+        return self.R + self.rope
+
+    @property
+    def dq(self) -> int:
+        return self.nope + self.rope
+
+    @property
+    def scale(self) -> float:
+        return 1.0 / math.sqrt(self.nope + self.rope)
+
+
+BASELINE = Geometry()
+
+
+def make_layer(seed: int, N: int, g: Geometry = BASELINE):
+    """One layer's inputs: q f32 (H, nope+rope), W_UK f16 (H, R, nope), kcache f16 (N, D),
+    W_UV f16 (H, V, R).  Each tensor draws from its own sub-seed."""
+    q = normal(seed * 8 + 1, g.H * g.dq).astype(np.float32).reshape(g.H, g.dq)
+    w_uk = (0.02 * normal(seed * 8 + 2, g.H * g.R * g.nope)).astype(np.float16).reshape(
+        g.H, g.R, g.nope)
+    kc = normal(seed * 8 + 3, N * g.D).astype(np.float16).reshape(N, g.D)
+    w_uv = (0.02 * normal(seed * 8 + 4, g.H * g.V * g.R)).astype(np.float16).reshape(
+        g.H, g.V, g.R)
+    return q, w_uk, kc, w_uv
+
+
+def window_mask(N: int, base: int, length: int) -> np.ndarray:
+    """The engine's mask: 0 on [base, base+length), -inf elsewhere (m1_layer.cpp:756-773)."""
+    m = np.full(N, -np.inf, np.float32)
+    lo, hi = max(base, 0), min(base + length, N)
+    if hi > lo:
+        m[lo:hi] = 0.0
+    return m
