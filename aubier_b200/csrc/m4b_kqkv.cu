@@ -7,20 +7,28 @@
 //   out[h]   = sum_n softmax_n(s[h][.]) * V[n]             V[n] = kcache row n, first 512 f16
 // All 32 heads share every KV row (MLA's latent cache), so per tile of 128 keys the work is two
 // dense products with the heads as the narrow dimension:
-//   MMA1  S^T[128 keys x 32 heads]   = Ktile[128 x 576] . Q^T[576 x 32]     (K-major A and B)
-//   MMA2  O^T[512 lat  x 32 heads]  += Vtile^T[512 x 128] . P[128 x 32]     (A read MN-major)
-// V is the first 512 columns of the SAME shared-memory tile MMA1 consumed, read through an
-// MN-major descriptor, so every KV byte crosses HBM exactly once.
+//   MMA1  S^T[128 keys x 32 heads]      = Ktile[128 x 576] . Q^T[576 x 32]    (K-major A and B)
+//   MMA2  O^T[128-latent block x 32]   += Vtile^T[128 x 128] . P[128 x 32]    (A read MN-major)
+// A tcgen05 MMA with N <= 64 costs the same ~65 cycles for M = 64 or 128, so both products use
+// M = 128 (128 keys, resp. 128 latent rows, per instruction): ~4.9k tensor cycles per tile.
+//
+// Shared memory cannot hold a 147 KB tile through its softmax AND the next tile, so the tile is
+// read twice: the K pass (all 576 columns, for MMA1) is released as soon as MMA1 consumed it,
+// and the V pass (the first 512 columns again, for MMA2) is re-read after the softmax -- from L2,
+// where the K pass left it (cache hint evict_last, re-read with evict_first).  HBM still sees
+// every KV byte once.  One FIFO ring of
+// five 32 KB slots carries, in consumption order, K(i+1) and V(i), so MMA1 of tile i+1 runs
+// while the softmax of tile i works (S and P are double-buffered).
 //
 // CTA = one split (a contiguous run of tiles, balanced as in m4-kqkv.cu:204-218), persistent,
 // one per SM.  Warp roles (320 threads):
-//   warp 0      TMA producer: per tile, the rope chunk (cols 512..575) then four 128-column
-//               "pairs" of the latent, into a 5-slot pair ring + 1 rope slot (smem 176 KB)
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warp 0      TMA producer (ring loads)
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer; descriptors are precomputed,
+//               each MMA costs one 32-bit add to issue
 //   warps 2..9  softmax: two groups of four warps, group g owns heads 16g..16g+15; warp w reads
 //               TMEM lanes 32*(w%4).. (one key per thread), does the online softmax in log2 units
 //               with a lazy rescale of O (only when a head's max grows by more than 2^8), writes
-//               P (f16) for MMA2, and writes the split's (o, m, l) partial at the end.
+//               P (f16) for MMA2, and writes the split's (o, m, l) partial record at the end.
 // Numerics: q and P are rounded to f16 for the tensor cores -- the same rounding points as the
 // reference CPU graph, whose mul_mat converts an F32 src1 to F16 (ggml-cpu.c:1330-1375) -- and
 // both products accumulate in f32.
@@ -35,35 +43,36 @@ namespace m4b {
 namespace kq {
 
 constexpr int H = kHeads;
-constexpr int D = kKRow;               // 576
-constexpr int TK = kTileKeys;          // 128 keys per tile
-constexpr int CHUNK_BYTES = TK * 128;  // 128 keys x 64 f16 columns = 16 KB (one SW128 atom column)
-constexpr int PAIR_BYTES = 2 * CHUNK_BYTES;
-constexpr int NPAIR = 5;               // latent ring: 5 x 32 KB
-constexpr int QCH_BYTES = H * 128;     // 32 heads x 64 columns f16 = 4 KB
-constexpr int NQCH = D / 64;           // 9
-constexpr int P_BYTES = 2 * QCH_BYTES; // 32 heads x 128 keys f16
+constexpr int D = kKRow;                // 576
+constexpr int TK = kTileKeys;           // 128 keys per tile
+constexpr int NCOL = D / 64;            // 9 column chunks per key row
+constexpr int CHUNK_BYTES = TK * 128;   // 128 keys x 64 f16 columns = 16 KB, one SW128 TMA box
+constexpr int SLOT_BYTES = 2 * CHUNK_BYTES;
+constexpr int NSLOT = 5;                // FIFO ring: 5 x 32 KB
+constexpr int K_ENTRIES = 5;            // K pass: column chunks (0,1) (2,3) (4,5) (6,7) (8)
+constexpr int V_ENTRIES = 4;            // V pass: column chunks (0,1) (2,3) (4,5) (6,7)
+constexpr int QCH_BYTES = H * 128;      // 32 heads x 64 columns f16 = 4 KB
+constexpr int P_BYTES = 2 * QCH_BYTES;  // 32 heads x 128 keys f16 = 8 KB (double-buffered)
 
-constexpr int OFF_PAIR = 0;
-constexpr int OFF_ROPE = OFF_PAIR + NPAIR * PAIR_BYTES;
-constexpr int OFF_Q = OFF_ROPE + CHUNK_BYTES;
-constexpr int OFF_P = OFF_Q + NQCH * QCH_BYTES;
-constexpr int OFF_CTRL = OFF_P + P_BYTES;
+constexpr int OFF_RING = 0;
+constexpr int OFF_Q = OFF_RING + NSLOT * SLOT_BYTES;
+constexpr int OFF_P = OFF_Q + NCOL * QCH_BYTES;
+constexpr int OFF_CTRL = OFF_P + 2 * P_BYTES;
 constexpr int CTRL_BYTES = 2048;
 constexpr int SMEM_BYTES = OFF_CTRL + CTRL_BYTES + 1024;  // + slack to align the base to 1 KB
 
 constexpr int NTHREADS = 320;
-constexpr int TMEM_COLS = 256;   // S^T: cols [0,32); O^T: cols [32,160) as 4 blocks of 32
+constexpr int TMEM_COLS = 256;   // S^T x2: cols [0,64); O^T: 4 blocks of 32 cols at [64,192)
 constexpr int TM_S = 0;
-constexpr int TM_O = 32;
+constexpr int TM_O = 64;
 constexpr float RESCALE_THRESH = 8.0f;  // log2 units: P stays <= 2^8 between rescales
 constexpr float LOG2E = 1.4426950408889634f;
 
 struct Ctrl {
-    uint64_t pair_full[NPAIR];
-    uint64_t pair_empty[NPAIR];
-    uint64_t rope_full, rope_empty;
-    uint64_t q_full, s_full, p_full, o_full;
+    uint64_t full[NSLOT];
+    uint64_t empty[NSLOT];
+    uint64_t s_full[2], p_full[2];
+    uint64_t q_full, o_done, o_full;
     uint64_t red_full[2];   // per head group: the 4 warps' tile maxima are in red[]
     uint64_t redl_full[2];  // per head group: the 4 warps' row sums are in red_l[]
     uint32_t tmem_base;
@@ -74,9 +83,10 @@ struct Ctrl {
 static_assert(sizeof(Ctrl) <= CTRL_BYTES, "control block too large");
 static_assert(offsetof(Ctrl, red) % 16 == 0 && offsetof(Ctrl, red_l) % 16 == 0,
               "reduction buffers are read with 16-byte vector loads");
-static_assert(OFF_CTRL % 16 == 0 && OFF_Q % 1024 == 0 && OFF_P % 1024 == 0 && OFF_ROPE % 1024 == 0,
+static_assert(OFF_Q % 1024 == 0 && OFF_P % 1024 == 0 && OFF_CTRL % 16 == 0,
               "TMA / UMMA operands need 1 KB alignment, vector accesses 16 B");
 static_assert(SMEM_BYTES <= 232448, "exceeds the 227 KB per-CTA shared memory of sm_100");
+static_assert(SMEM_BYTES < (1 << 18), "descriptor low halves assume shared addresses < 256 KB");
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
@@ -132,20 +142,19 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
     const int nt = base_t + (split < rem ? 1 : 0);
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < NPAIR; ++i) {
-            mbar_init(&C.pair_full[i], 1);
-            mbar_init(&C.pair_empty[i], 1);
+        for (int i = 0; i < NSLOT; ++i) {
+            mbar_init(&C.full[i], 1);
+            mbar_init(&C.empty[i], 1);
         }
-        mbar_init(&C.rope_full, 1);
-        mbar_init(&C.rope_empty, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&C.s_full[b], 1);
+            mbar_init(&C.p_full[b], 8);
+            mbar_init(&C.red_full[b], 4);
+            mbar_init(&C.redl_full[b], 4);
+        }
         mbar_init(&C.q_full, 256);
-        mbar_init(&C.s_full, 1);
-        mbar_init(&C.p_full, 8);
+        mbar_init(&C.o_done, 1);
         mbar_init(&C.o_full, 1);
-        for (int g = 0; g < 2; ++g) {
-            mbar_init(&C.red_full[g], 4);
-            mbar_init(&C.redl_full[g], 4);
-        }
         C.abort_flag = 0;
         fence_mbar_init();
     }
@@ -164,34 +173,38 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
         // ------------------------------------------------------------------ TMA producer
         if (lane == 0) {
             if (!(flags & M4B_FLAG_KV_STATIC)) pdl_wait();
-            const uint64_t pol = l2_policy_evict_first();
+            const uint64_t pol_keep = l2_policy_evict_last();    // K pass: V is re-read soon
+            const uint64_t pol_done = l2_policy_evict_first();   // V pass: last use
+            int slot = 0, phase = 0, issued = 0;
             bool ok = true;
-            int rope_issued = 0, pair_issued = 0;
-            for (int i = 0; i < nt && ok; ++i) {
-                const int key0 = (t0 + i) * TK;
-                ok = mbar_wait(&C.rope_empty, (i & 1) ^ 1, abort_flag);
-                if (!ok) break;
-                mbar_arrive_expect_tx(&C.rope_full, CHUNK_BYTES);
-                tma_load_2d(smem + OFF_ROPE, &tmap, kLatent, key0, &C.rope_full, pol);
-                ++rope_issued;
-                for (int p = 0; p < 4 && ok; ++p) {
-                    const int g = 4 * i + p;
-                    const int slot = g % NPAIR;
-                    ok = mbar_wait(&C.pair_empty[slot], ((g / NPAIR) & 1) ^ 1, abort_flag);
-                    if (!ok) break;
-                    mbar_arrive_expect_tx(&C.pair_full[slot], PAIR_BYTES);
-                    uint8_t* dst = smem + OFF_PAIR + slot * PAIR_BYTES;
-                    tma_load_2d(dst, &tmap, 128 * p, key0, &C.pair_full[slot], pol);
-                    tma_load_2d(dst + CHUNK_BYTES, &tmap, 128 * p + 64, key0, &C.pair_full[slot], pol);
-                    ++pair_issued;
+            // one ring entry: chunks c0 (and c0 + 1 when two) of tile t
+            auto entry = [&](int t, int c0, int two, uint64_t pol) {
+                ok = ok && mbar_wait(&C.empty[slot], phase ^ 1, abort_flag);
+                if (!ok) return;
+                mbar_arrive_expect_tx(&C.full[slot], two ? SLOT_BYTES : CHUNK_BYTES);
+                uint8_t* dst = smem + OFF_RING + slot * SLOT_BYTES;
+                const int key0 = (t0 + t) * TK;
+                tma_load_2d(dst, &tmap, 64 * c0, key0, &C.full[slot], pol);
+                if (two) tma_load_2d(dst + CHUNK_BYTES, &tmap, 64 * (c0 + 1), key0, &C.full[slot], pol);
+                ++issued;
+                if (++slot == NSLOT) {
+                    slot = 0;
+                    phase ^= 1;
                 }
+            };
+            // ring order = consumption order: K(0), then per tile i: K(i+1), V(i)
+            for (int t = -1; t < nt && ok; ++t) {
+                if (t + 1 < nt) {
+                    for (int e = 0; e < K_ENTRIES; ++e) entry(t + 1, 2 * e, e < 4, pol_keep);
+                }
+                if (t >= 0)
+                    for (int e = 0; e < V_ENTRIES; ++e) entry(t, 2 * e, 1, pol_done);
             }
             if (*abort_flag) {
                 // let this CTA's own copies land before its shared memory is released
-                if (rope_issued > 0) mbar_drain(&C.rope_full, (rope_issued - 1) & 1);
-                for (int slot = 0; slot < NPAIR; ++slot) {
-                    const int n = pair_issued > slot ? (pair_issued - slot + NPAIR - 1) / NPAIR : 0;
-                    if (n > 0) mbar_drain(&C.pair_full[slot], (n - 1) & 1);
+                for (int sl = 0; sl < NSLOT; ++sl) {
+                    const int n = issued > sl ? (issued - sl + NSLOT - 1) / NSLOT : 0;
+                    if (n > 0) mbar_drain(&C.full[sl], (n - 1) & 1);
                 }
             }
         }
@@ -200,58 +213,69 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
         if (lane == 0) {
             constexpr uint32_t idesc_s = idesc_f16_f32(128, 32, false, false);
             constexpr uint32_t idesc_o = idesc_f16_f32(128, 32, true, false);
-            const uint32_t q_base = smem_u32(smem + OFF_Q);
-            const uint32_t p_base = smem_u32(smem + OFF_P);
-            const uint32_t rope_base = smem_u32(smem + OFF_ROPE);
-            const uint32_t pair_base = smem_u32(smem + OFF_PAIR);
-            const uint32_t tS = tmem + TM_S;
-            const uint32_t tO = tmem + TM_O;
+            constexpr uint32_t hi = sdesc_sw128_hi(1024);   // SBO = 8 rows x 128 B
+            // low descriptor halves; offsets below are in 16-byte units
+            const uint32_t lo_ringK = sdesc_sw128_lo(smem_u32(smem + OFF_RING), 16);
+            const uint32_t lo_ringMN = sdesc_sw128_lo(smem_u32(smem + OFF_RING), CHUNK_BYTES);
+            const uint32_t lo_q = sdesc_sw128_lo(smem_u32(smem + OFF_Q), 16);
+            const uint32_t lo_p = sdesc_sw128_lo(smem_u32(smem + OFF_P), 16);
+            constexpr uint32_t U_CHUNK = CHUNK_BYTES >> 4, U_SLOT = SLOT_BYTES >> 4;
+            constexpr uint32_t U_QCH = QCH_BYTES >> 4, U_P = P_BYTES >> 4;
+            int slot = 0, phase = 0;
             bool ok = mbar_wait(&C.q_full, 0, abort_flag);
-            for (int i = 0; i < nt && ok; ++i) {
-                // MMA1: S^T = Ktile . Q^T over the 9 column chunks (rope chunk first)
-                ok = mbar_wait(&C.rope_full, i & 1, abort_flag);
-                if (!ok) break;
-                tc_fence_after();
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_f16(tS, sdesc_sw128(rope_base + kk * 32, 16, 1024),
-                            sdesc_sw128(q_base + 8 * QCH_BYTES + kk * 32, 16, 1024), idesc_s,
-                            kk > 0 ? 1u : 0u);
-                mma_commit(&C.rope_empty);
-                for (int p = 0; p < 4 && ok; ++p) {
-                    const int g = 4 * i + p;
-                    const int slot = g % NPAIR;
-                    ok = mbar_wait(&C.pair_full[slot], (g / NPAIR) & 1, abort_flag);
+            auto take = [&]() -> uint32_t {   // wait for the next ring entry, return its slot
+                const uint32_t s_ = slot;
+                ok = ok && mbar_wait(&C.full[slot], phase, abort_flag);
+                if (++slot == NSLOT) {
+                    slot = 0;
+                    phase ^= 1;
+                }
+                return s_;
+            };
+            // MMA1 of tile t into S[t & 1]
+            auto mma1 = [&](int t) {
+                const uint32_t dS = tmem + TM_S + 32 * (t & 1);
+                for (int e = 0; e < K_ENTRIES && ok; ++e) {
+                    const uint32_t sl = take();
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t pb = pair_base + slot * PAIR_BYTES;
+                    const uint32_t a = lo_ringK + sl * U_SLOT;
+                    const uint32_t b = lo_q + 2 * e * U_QCH;
 #pragma unroll
                     for (int hf = 0; hf < 2; ++hf) {
-                        const int c = 2 * p + hf;
+                        if (hf == 1 && e == 4) break;
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)
-                            mma_f16(tS, sdesc_sw128(pb + hf * CHUNK_BYTES + kk * 32, 16, 1024),
-                                    sdesc_sw128(q_base + c * QCH_BYTES + kk * 32, 16, 1024),
-                                    idesc_s, 1u);
+                            mma_f16(dS, sdesc_join(a + hf * U_CHUNK + 2 * kk, hi),
+                                    sdesc_join(b + hf * U_QCH + 2 * kk, hi), idesc_s,
+                                    (e | hf | kk) != 0 ? 1u : 0u);
                     }
+                    mma_commit(&C.empty[sl]);
                 }
-                if (!ok) break;
-                mma_commit(&C.s_full);
-                // MMA2: O^T[128-latent block b] += Vtile^T . P, V read MN-major from the pair
-                ok = mbar_wait(&C.p_full, i & 1, abort_flag);
+                if (ok) mma_commit(&C.s_full[t & 1]);
+            };
+            if (nt > 0) mma1(0);
+            for (int i = 0; i < nt && ok; ++i) {
+                if (i + 1 < nt) mma1(i + 1);
+                // MMA2 of tile i: needs its P, then the 4 latent blocks of the V pass
+                ok = ok && mbar_wait(&C.p_full[i & 1], (i >> 1) & 1, abort_flag);
                 if (!ok) break;
                 tc_fence_after();
-                for (int b = 0; b < 4; ++b) {
-                    const int g = 4 * i + b;
-                    const int slot = g % NPAIR;
-                    const uint32_t pb = pair_base + slot * PAIR_BYTES;
+                const uint32_t b0 = lo_p + (i & 1) * U_P;
+                const uint32_t acc0 = i > 0 ? 1u : 0u;
+                for (int b = 0; b < V_ENTRIES && ok; ++b) {
+                    const uint32_t sl = take();
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t a0 = lo_ringMN + sl * U_SLOT;
 #pragma unroll
                     for (int ks = 0; ks < 8; ++ks)
-                        mma_f16(tO + 32 * b, sdesc_sw128(pb + ks * 2048, CHUNK_BYTES, 1024),
-                                sdesc_sw128(p_base + (ks >> 2) * QCH_BYTES + (ks & 3) * 32, 16, 1024),
-                                idesc_o, (i > 0 || ks > 0) ? 1u : 0u);
-                    mma_commit(&C.pair_empty[slot]);
+                        mma_f16(tmem + TM_O + 32 * b, sdesc_join(a0 + ks * (2048 >> 4), hi),
+                                sdesc_join(b0 + (ks >> 2) * U_QCH + 2 * (ks & 3), hi), idesc_o,
+                                ks > 0 ? 1u : acc0);
+                    mma_commit(&C.empty[sl]);
                 }
+                mma_commit(&C.o_done);
             }
             mma_commit(&C.o_full);
         }
@@ -260,7 +284,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
         const int sw = warp - 2;       // 0..7
         const int grp = sw >> 2;       // heads 16*grp .. 16*grp+15
         const int quad = warp & 3;     // TMEM lane quadrant this warp may access
-        const int key_in_tile = quad * 32 + lane;
+        const int key_in_tile = quad * 32 + lane;   // M = 128 layout: lane = row
         const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
 
         // Stage Q (f32 -> f16, round to nearest even) into the K-major SW128 layout.
@@ -282,11 +306,10 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
         fence_proxy_async_smem();
         mbar_arrive(&C.q_full);
 
-        // P destination of this thread's key (column key_in_tile of 32 head rows)
-        const int pchunk = key_in_tile >> 6;
-        const int pkk = key_in_tile & 63;
-        uint8_t* const prow0 = smem + OFF_P + pchunk * QCH_BYTES + (pkk & 7) * 2;
-        const int punit = pkk >> 3;
+        // P destination of this thread's key: column key_in_tile of the 32 head rows, K-major,
+        // as two 64-key chunks of 4 KB
+        uint8_t* const prow0 = smem + OFF_P + (key_in_tile >> 6) * QCH_BYTES + (key_in_tile & 7) * 2;
+        const int punit = (key_in_tile & 63) >> 3;
 
         float m_run[16], l_part[16];
 #pragma unroll
@@ -300,11 +323,11 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
             const bool valid = kg < n_kv;
             float mv = 0.0f;
             if (valid && mask != nullptr) mv = __ldg(mask + kg);
-            ok = warp_wait(&C.s_full, i & 1, abort_flag);
+            ok = warp_wait(&C.s_full[i & 1], (i >> 1) & 1, abort_flag);
             if (!ok) break;
             tc_fence_after();
             float s[16];
-            tmem_ld16(tmem + lane_off + TM_S + 16 * grp, s);
+            tmem_ld16(tmem + lane_off + TM_S + 32 * (i & 1) + 16 * grp, s);
             tmem_wait_ld();
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -351,6 +374,10 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
                 }
             }
             if (need) {   // uniform across the group: every thread computed the same maxima
+                // O holds the sum through tile i-1: wait for MMA2(i-1) before rescaling it
+                ok = warp_wait(&C.o_done, (i - 1) & 1, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
 #pragma unroll
                 for (int j = 0; j < 16; ++j) l_part[j] *= alpha[j];
 #pragma unroll
@@ -365,18 +392,19 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
                 }
                 tmem_wait_st();
             }
+            uint8_t* const prow = prow0 + (i & 1) * P_BYTES;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const float p = (s[j] == -INFINITY) ? 0.0f : exp2f(s[j] - m_run[j]);
                 l_part[j] += p;
                 const int h = 16 * grp + j;
-                *reinterpret_cast<__half*>(prow0 + h * 128 + ((punit ^ (h & 7)) << 4)) =
+                *reinterpret_cast<__half*>(prow + h * 128 + ((punit ^ (h & 7)) << 4)) =
                     __float2half_rn(p);
             }
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&C.p_full);
+            if (lane == 0) mbar_arrive(&C.p_full[i & 1]);
         }
 
         // ---- epilogue: the split's partial record (o[512], m, l) per head
@@ -406,7 +434,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
                 float o[16];
                 tmem_ld16(tmem + lane_off + TM_O + 32 * b + 16 * grp, o);
                 tmem_wait_ld();
-                const int d = 128 * b + quad * 32 + lane;
+                const int d = 128 * b + quad * 32 + lane;   // M = 128 layout: every lane is a row
 #pragma unroll
                 for (int j = 0; j < 16; ++j) prec[(16 * grp + j) * kPartStride + d] = o[j];
             }
@@ -421,47 +449,69 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
     }
 }
 
-// Merge S partial records per head (m4-kqkv.cu:318-338 rule, log2 units); one thread per
-// output element, grid (heads, latent / 128).
-__global__ void __launch_bounds__(128)
+// Merge S partial records per head with the online-softmax rule of m4-kqkv.cu:318-338 (log2
+// units here): m* = max m_s; a_s = 2^(m_s - m*); out = sum a_s o_s / sum a_s l_s; a head whose
+// every split is fully masked gives 0.  CTA = (head, 128 latent columns); the 8 warps split the
+// records, each lane accumulates 4 columns with 16-byte loads, one reduction through shared
+// memory at the end.  S may exceed one GPU's split count (records gathered from other GPUs).
+constexpr int CMB_THREADS = 256;
+
+__global__ void __launch_bounds__(CMB_THREADS)
 kqkv_combine_kernel(const float* __restrict__ part, int S, float* __restrict__ out, int64_t out_hs) {
+    extern __shared__ float s_alpha[];   // [S]
+    __shared__ float s_red[CMB_THREADS / 32][128];
+    __shared__ float s_m[CMB_THREADS / 32], s_l[CMB_THREADS / 32];
     pdl_wait();
     const int h = blockIdx.x;
-    const int d = blockIdx.y * 128 + threadIdx.x;
-    const float* ph = part + static_cast<size_t>(h) * kPartStride;
+    const int d0 = blockIdx.y * 128;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const size_t ss = static_cast<size_t>(H) * kPartStride;
-    float mstar = -INFINITY;
-    for (int s = 0; s < S; ++s) mstar = fmaxf(mstar, __ldg(ph + s * ss + kPartM));
-    float l = 0.0f, o = 0.0f;
-    if (mstar > -INFINITY) {
-        int s = 0;
-        for (; s + 4 <= S; s += 4) {
-            float m4[4], l4[4], o4[4];
+    const float* ph = part + static_cast<size_t>(h) * kPartStride;
+
+    float m = -INFINITY;
+    for (int s = tid; s < S; s += CMB_THREADS) m = fmaxf(m, __ldg(ph + s * ss + kPartM));
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                m4[u] = __ldg(ph + (s + u) * ss + kPartM);
-                l4[u] = __ldg(ph + (s + u) * ss + kPartL);
-                o4[u] = __ldg(ph + (s + u) * ss + d);
-            }
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (lane == 0) s_m[warp] = m;
+    __syncthreads();
+    float mstar = s_m[0];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                if (m4[u] > -INFINITY) {
-                    const float a = exp2f(m4[u] - mstar);
-                    l += l4[u] * a;
-                    o += o4[u] * a;
-                }
-            }
-        }
-        for (; s < S; ++s) {
-            const float m = __ldg(ph + s * ss + kPartM);
-            if (m > -INFINITY) {
-                const float a = exp2f(m - mstar);
-                l += __ldg(ph + s * ss + kPartL) * a;
-                o += __ldg(ph + s * ss + d) * a;
-            }
-        }
+    for (int w = 1; w < CMB_THREADS / 32; ++w) mstar = fmaxf(mstar, s_m[w]);
+
+    float lsum = 0.0f;
+    for (int s = tid; s < S; s += CMB_THREADS) {
+        const float ms = __ldg(ph + s * ss + kPartM);
+        const float a = (ms > -INFINITY) ? exp2f(ms - mstar) : 0.0f;
+        s_alpha[s] = a;
+        lsum += a * __ldg(ph + s * ss + kPartL);
     }
-    out[h * out_hs + d] = (mstar > -INFINITY) ? o / l : 0.0f;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
+    if (lane == 0) s_l[warp] = lsum;
+    __syncthreads();
+
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* col = ph + d0 + 4 * lane;
+#pragma unroll 4
+    for (int s = warp; s < S; s += CMB_THREADS / 32) {
+        const float a = s_alpha[s];
+        const float4 v = __ldg(reinterpret_cast<const float4*>(col + s * ss));
+        acc.x = fmaf(a, v.x, acc.x);
+        acc.y = fmaf(a, v.y, acc.y);
+        acc.z = fmaf(a, v.z, acc.z);
+        acc.w = fmaf(a, v.w, acc.w);
+    }
+    *reinterpret_cast<float4*>(&s_red[warp][4 * lane]) = acc;
+    __syncthreads();
+    if (tid < 128) {
+        float o = 0.0f, l = 0.0f;
+#pragma unroll
+        for (int w = 0; w < CMB_THREADS / 32; ++w) {
+            o += s_red[w][tid];
+            l += s_l[w];
+        }
+        out[h * out_hs + d0 + tid] = (mstar > -INFINITY) ? o / l : 0.0f;
+    }
 }
 
 }  // namespace kq
@@ -506,8 +556,10 @@ cudaError_t launch_kqkv_partials(const KqkvLaunch& a, cudaStream_t stream) {
 
 cudaError_t launch_kqkv_combine(const float* part, int S, float* out, int64_t out_hs,
                                 uint32_t flags, cudaStream_t stream) {
-    return launch(kq::kqkv_combine_kernel, dim3(kHeads, kLatent / 128), dim3(128), 0, stream, flags,
-                  part, S, out, out_hs);
+    const size_t smem = static_cast<size_t>(S) * sizeof(float);
+    if (smem > 48 * 1024) return cudaErrorInvalidValue;   // > 12288 records: not a real config
+    return launch(kq::kqkv_combine_kernel, dim3(kHeads, kLatent / 128), dim3(kq::CMB_THREADS), smem,
+                  stream, flags, part, S, out, out_hs);
 }
 
 }  // namespace m4b

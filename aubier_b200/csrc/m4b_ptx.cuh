@@ -61,6 +61,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking test (never suspends the thread): for a single thread polling several barriers.
+__device__ __forceinline__ bool mbar_test(uint32_t addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity.  Returns false (and raises the abort flag)
 // when the limit passes or another role already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
@@ -98,6 +111,12 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
     return p;
 }
 
@@ -162,6 +181,19 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, ui
     d |= 1ull << 46;   // descriptor version for tcgen05
     d |= 2ull << 61;   // layout: SWIZZLE_128B
     return d;
+}
+
+// The same descriptor split into 32-bit halves: only the low half depends on the address, and
+// for a shared-memory address below 256 KB adding (offset >> 4) to it never carries into the
+// high half, so a hot loop can advance a descriptor with one 32-bit add.
+__host__ __device__ constexpr uint32_t sdesc_sw128_lo(uint32_t saddr, uint32_t lbo) {
+    return ((saddr >> 4) & 0x3FFFu) | (((lbo >> 4) & 0x3FFFu) << 16);
+}
+__host__ __device__ constexpr uint32_t sdesc_sw128_hi(uint32_t sbo) {
+    return ((sbo >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
+}
+__device__ __forceinline__ uint64_t sdesc_join(uint32_t lo, uint32_t hi) {
+    return (static_cast<uint64_t>(hi) << 32) | lo;
 }
 
 // Instruction descriptor for kind::f16 with f16 A/B and f32 accumulation.

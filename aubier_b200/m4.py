@@ -31,6 +31,7 @@ LIB_PATH = os.path.join(_PKG, "libm4b.so")
 HEADS, NOPE, ROPE, LATENT, VHEAD = 32, 128, 64, 512, 128
 KROW = LATENT + ROPE
 PART_STRIDE = LATENT + 4   # o[512], m (log2 units), l, 2 pad
+TILE_KEYS = 128            # keys per KQKV tile: splits are balanced over ceil(N / 128) tiles
 
 F32, F16, Q8_0, I32, I64 = 0, 1, 8, 26, 27
 FLAG_PDL, FLAG_KV_STATIC = 1, 2

@@ -129,7 +129,8 @@ M4B_API int m4b_kqkv(const m4b_kqkv_args * args, m4b_stream_t stream);
  * KQKV, split-K partials only (no reference counterpart: the additive op the multi-GPU and fused
  * paths use; the partial is the (m, l, o) record of m4-kqkv.cu:306-311).
  *   dst  partials F32 [516, 32, S, 1] contiguous: per (split, head) o[512] then m (log2 units),
- *        l, 2 pad floats.  1 <= S <= min(m4b_kqkv_max_splits(), ceil(N / 128)).
+ *        l, 2 pad floats.  1 <= S <= min(m4b_kqkv_max_splits(), ceil(N / 128)); split s
+ *        covers a balanced contiguous run of 128-key tiles.
  * src0..src2 and kq_scale as for m4b_kqkv; scratch unused.
  */
 M4B_API int m4b_kqkv_partials(const m4b_kqkv_args * args, m4b_stream_t stream);

@@ -10,6 +10,7 @@ Run from the repository root (needs oracle/_ref built):  python tests/golden/mak
 """
 from __future__ import annotations
 
+import hashlib
 import json
 import os
 import sys
@@ -61,7 +62,11 @@ def main() -> None:
         ref.close()
         np.savez_compressed(os.path.join(out_dir, f"{name}.npz"), q_abs=q_abs, qcur=qcur,
                             attn=attn, out=out)
+        h = hashlib.sha256()
+        for a in (q, w_uk, kc, w_uv):
+            h.update(np.ascontiguousarray(a).tobytes())
         index[name] = {"seed": seed, "N": N, "mask": list(spec), "graph_nodes": n_nodes,
+                       "inputs_sha256_16": h.hexdigest()[:16],
                        "geometry": {"H": g.H, "nope": g.nope, "rope": g.rope, "R": g.R, "V": g.V},
                        "scale": g.scale}
         print(name, N, "nodes", n_nodes, "max|out|", float(np.abs(out).max()))

@@ -1,0 +1,172 @@
+"""CPU tests of the C ABI and the host-side mirror: the library loads and exports every symbol
+include/m4b.h declares, contract checks reject bad operands before any CUDA call, supports_op
+mirrors the reference's per-op contract, and the tri-state flag resolves as the engine does.
+No test here launches anything."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from aubier_b200 import m4
+from aubier_b200.shard import kv_slabs, lpt_assign, rank_loads
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "m4b.h")
+FAKE = 0x7F0000000000   # a 4 KB-aligned non-null address; never dereferenced by these tests
+
+
+def declared_symbols():
+    with open(HEADER) as f:
+        text = f.read()
+    return sorted(set(re.findall(r"M4B_API\s+[\w\s\*]+?\b(m4b_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    names = declared_symbols()
+    assert len(names) >= 13
+    lib = ctypes.CDLL(m4.LIB_PATH)
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in include/m4b.h but not exported"
+
+
+def test_abi_version_and_strerror():
+    assert m4.abi_version() == 1
+    for code in range(7):
+        assert m4.strerror(code).startswith("ok") or m4.strerror(code).startswith("m4b")
+    assert "unknown" in m4.strerror(99)
+
+
+def T(type_id, ne, nb, addr=FAKE):
+    t = m4.Tensor()
+    t.data = addr
+    t.type = type_id
+    for i in range(4):
+        t.ne[i] = ne[i]
+        t.nb[i] = nb[i]
+    return t
+
+
+def contiguous(type_id, ne, esz):
+    nb = [esz]
+    for i in range(1, 4):
+        nb.append(nb[-1] * ne[i - 1])
+    return T(type_id, ne, nb)
+
+
+N = 1000
+WUK = contiguous(m4.F16, [128, 512, 32, 1], 2)
+QNOPE = T(m4.F32, [128, 32, 1, 1], [4, 768, 768 * 32, 768 * 32])
+QABS = contiguous(m4.F32, [512, 32, 1, 1], 4)
+KC = contiguous(m4.F16, [576, N, 1, 1], 2)
+QCUR = contiguous(m4.F32, [576, 32, 1, 1], 4)
+MASK = contiguous(m4.F32, [N, 1, 1, 1], 4)
+ATTN = T(m4.F32, [512, 1, 32, 1], [4, 2048, 2048, 2048 * 32])
+WUV = contiguous(m4.F16, [512, 128, 32, 1], 2)
+OUT = T(m4.F32, [128, 1, 32, 1], [4, 512, 512, 512 * 32])
+PARTS = contiguous(m4.F32, [516, 32, 7, 1], 4)
+
+
+def test_supports_op_accepts_the_baseline_contract():
+    assert m4.supports_op(m4.OP_WKB, [WUK, QNOPE], QABS)
+    assert m4.supports_op(m4.OP_KQKV, [KC, QCUR, MASK], ATTN)
+    assert m4.supports_op(m4.OP_KQKV, [KC, QCUR], ATTN)              # mask optional
+    assert m4.supports_op(m4.OP_PHASE, [WUV, ATTN], OUT, [1] + [0] * 15)
+    assert m4.supports_op(m4.OP_PHASE, [WUV, PARTS], OUT, [2] + [0] * 15)
+
+
+def test_supports_op_rejects_contract_violations():
+    bad_kc = contiguous(m4.F32, [576, N, 1, 1], 4)                     # cache must be F16
+    assert not m4.supports_op(m4.OP_KQKV, [bad_kc, QCUR, MASK], ATTN)
+    bad_mask = contiguous(m4.F32, [N - 1, 1, 1, 1], 4)                 # mask ne0 != n_kv
+    assert not m4.supports_op(m4.OP_KQKV, [KC, QCUR, bad_mask], ATTN)
+    odd_row = T(m4.F16, [576, N, 1, 1], [2, 1160, 1160 * N, 1160 * N])  # row not 16-B multiple
+    assert not m4.supports_op(m4.OP_KQKV, [odd_row, QCUR, MASK], ATTN)
+    unaligned = contiguous(m4.F16, [576, N, 1, 1], 2)
+    unaligned.data = FAKE + 8                                          # TMA needs 16-B alignment
+    assert not m4.supports_op(m4.OP_KQKV, [unaligned, QCUR, MASK], ATTN)
+    assert not m4.supports_op(m4.OP_WKB, [WUK, contiguous(m4.F32, [128, 16, 1, 1], 4)], QABS)
+    assert not m4.supports_op(m4.OP_PHASE, [WUV, ATTN], OUT, [3] + [0] * 15)   # unknown phase
+    assert not m4.supports_op(m4.OP_PHASE, [WUV, ATTN], OUT, [0] + [0] * 15)   # kvwrite: Mistral
+    q8 = contiguous(m4.Q8_0, [64, 256, 32, 1], 1)                      # Mistral W_UK: not here yet
+    assert not m4.supports_op(m4.OP_WKB, [q8, QNOPE], QABS)
+
+
+def _call(fn, args):
+    return fn(ctypes.byref(args), ctypes.c_void_p(0))
+
+
+def test_entry_points_refuse_bad_operands_before_any_cuda_call():
+    lib = m4.lib()
+    a = m4.KqkvArgs()
+    a.src0, a.src1, a.src2, a.dst = contiguous(m4.F32, [576, N, 1, 1], 4), QCUR, MASK, ATTN
+    a.kq_scale = 0.07
+    assert _call(lib.m4b_kqkv, a) == m4.EINVAL
+    a.src0 = KC
+    a.kq_scale = float("nan")
+    assert _call(lib.m4b_kqkv, a) == m4.EINVAL
+    w = m4.WkbArgs()
+    w.src0, w.src1, w.dst = WUK, QNOPE, contiguous(m4.F32, [256, 32, 1, 1], 4)
+    assert _call(lib.m4b_wkb, w) == m4.EINVAL
+    p = m4.PhaseArgs()
+    p.src[0], p.src[1], p.dst = WUV, ATTN, OUT
+    p.op_params[0] = 7
+    assert _call(lib.m4b_phase, p) == m4.EINVAL
+    p.op_params[0] = 0
+    assert _call(lib.m4b_phase, p) == m4.ENOTSUP
+    assert lib.m4b_kqkv(None, None) == m4.EINVAL
+
+
+def test_scratch_sizes():
+    assert m4.kqkv_scratch_bytes(262144) == 148 * 32 * 516 * 4
+    assert m4.kqkv_scratch_bytes(4096) == 32 * 32 * 516 * 4
+    assert m4.kqkv_scratch_bytes(1) == 32 * 516 * 4
+    assert m4.lib().m4b_phase_scratch_bytes(2) == 32 * 512 * 4
+    assert m4.lib().m4b_kqkv_max_splits() == 148
+
+
+@pytest.mark.parametrize("flag,gpu,nt,ragged,want", [
+    (-1, 1, 1, 0, True), (-1, 0, 1, 0, False), (0, 1, 1, 0, False), (1, 1, 1, 0, True),
+    (-1, 1, 4, 0, False), (-1, 1, 4, 1, True), (0, 0, 1, 0, False)])
+def test_tristate_flag_resolution(flag, gpu, nt, ragged, want):
+    assert m4.resolve_flag(flag, gpu, nt, ragged) is want
+
+
+@pytest.mark.parametrize("flag,gpu,nt", [(1, 0, 1), (1, 1, 4), (2, 1, 1), (-2, 1, 1)])
+def test_tristate_flag_refusals(flag, gpu, nt):
+    with pytest.raises(m4.M4Error) as e:
+        m4.resolve_flag(flag, gpu, nt)
+    assert e.value.code == m4.EINVAL
+
+
+def test_host_tensors_have_no_cpu_handler():
+    kc = torch.zeros(16, 576, dtype=torch.float16)
+    q = torch.zeros(32, 576)
+    with pytest.raises(m4.M4Error, match="no CPU handler"):
+        m4.kqkv(kc, q, None, 0.07)
+    with pytest.raises(m4.M4Error, match="no CPU handler"):
+        m4.wkb(torch.zeros(32, 512, 128, dtype=torch.float16), torch.zeros(32, 192)[:, :128])
+
+
+def test_kv_slabs_cover_the_context():
+    for n, w in [(262144, 1), (262144, 2), (262144, 8), (1000, 3), (5, 4), (0, 2)]:
+        slabs = kv_slabs(n, w)
+        assert len(slabs) == w and slabs[0][0] == 0 and slabs[-1][1] == n
+        for (b0, e0), (b1, e1) in zip(slabs, slabs[1:]):
+            assert e0 == b1
+        tiles = [(e - b + 127) // 128 for b, e in slabs]
+        assert max(tiles) - min(tiles) <= 1          # balanced to one 128-key tile
+
+
+def test_lpt_balances_ragged_batches():
+    lengths = [512, 65536, 4000, 30000, 777, 12345, 65000, 2048, 9999, 40000, 600, 31000,
+               8000, 15000, 50000, 1234]
+    for w in (1, 2, 4, 8):
+        a = lpt_assign(lengths, w)
+        assert sorted(i for r in a for i in r) == list(range(len(lengths)))
+        loads = rank_loads(lengths, a)
+        # LPT bound: makespan <= 4/3 OPT; OPT >= max(total / w, max length)
+        opt_lb = max(sum(lengths) / w, max(lengths))
+        assert max(loads) <= 4 / 3 * opt_lb + 1
+    assert lpt_assign(lengths, 4) == lpt_assign(list(lengths), 4)   # deterministic
