@@ -4,3 +4,4 @@
 #include "m4b_kqkv.cu"
 #include "m4b_gemv.cu"
 #include "m4b_api.cu"
+#include "m4b_noalloc.cu"

@@ -136,6 +136,18 @@ M4B_API int m4b_kqkv(const m4b_kqkv_args * args, m4b_stream_t stream);
 M4B_API int m4b_kqkv_partials(const m4b_kqkv_args * args, m4b_stream_t stream);
 
 /*
+ * KQKV for callers that cannot allocate (no counterpart in the reference, whose KQKV always uses
+ * its own static array; here the regular entry point takes caller scratch instead).  Same
+ * operands, contract and output as m4b_kqkv; args->scratch is ignored.  The split-K partial
+ * records live in a fixed device array inside the library (148 splits x 32 heads x 2064 B =
+ * 9.8 MB per GPU, held until exit); a call needing more records returns M4B_ESCRATCH.  The first
+ * call on a device looks the array's address up (cudaGetSymbolAddress) with that device current:
+ * make it before any stream capture.  Calls on one device share the array: calls whose kernels
+ * overlap on the GPU race.  Allocates nothing (no cudaMalloc / cudaFree).
+ */
+M4B_API int m4b_kqkv_static_scratch(const m4b_kqkv_args * args, m4b_stream_t stream);
+
+/*
  * GGML_OP_M4_PHASE -- the remaining per-token phases, selected by op_params[0].
  * Replaces ggml_cuda_m4_phase (patches/ggml-m4/m4-phase.cu:205-277); builders
  * ggml_m4_phase_kvwrite / ggml_m4_phase_wvb (ggml.c:3461-3539).
