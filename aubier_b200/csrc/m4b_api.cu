@@ -190,6 +190,15 @@ int check_phase(const m4b_phase_args& a) {
             if (a.src[2].data != nullptr && check_attn(a.src[2]) != M4B_OK) return M4B_EINVAL;
             return check_phase_dst(a.dst);
         }
+        case 3: {   // merge records -> one record per head (additive, for the GPU exchange)
+            int rc = check_partials(a.src[1], 0);
+            if (rc != M4B_OK) return rc;
+            const m4b_tensor& d = a.dst;
+            if (d.type != M4B_TYPE_F32 || d.ne[0] != kPartStride || d.ne[1] != kHeads ||
+                d.ne[2] != 1 || d.ne[3] != 1 || !packed3(d, 4) || !d.data || !aligned(d.data, 16))
+                return M4B_EINVAL;
+            return M4B_OK;
+        }
         default:   // m4-phase.cu:276 GGML_ABORT("unknown phase")
             return M4B_EINVAL;
     }
@@ -314,6 +323,11 @@ int m4b_phase(const m4b_phase_args* a, m4b_stream_t stream) {
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     float* out = static_cast<float*>(a->dst.data);
     const int64_t out_hs = static_cast<int64_t>(a->dst.nb[2] / 4);
+    if (phase == 3) {
+        return status_of(launch_kqkv_merge_records(static_cast<const float*>(a->src[1].data),
+                                                   static_cast<int>(a->src[1].ne[2]), out,
+                                                   a->flags & M4B_FLAG_PDL, s));
+    }
     if (phase == 1) {
         return status_of(launch_wvb_f16(a->src[0].data, static_cast<const float*>(a->src[1].data),
                                         static_cast<int64_t>(a->src[1].nb[2] / 4), out, out_hs,

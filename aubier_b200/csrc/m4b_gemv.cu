@@ -9,7 +9,10 @@
 // Reference kernels replaced: m4-wkb.cu:55-69 (Q8_0 geometry) and m4-phase.cu:52-89.
 //
 // PDL: the weight rows do not depend on the preceding kernel, so they are loaded into registers
-// BEFORE griddepcontrol.wait; only the activation read waits.
+// BEFORE griddepcontrol.wait; only the activation read waits.  No kernel releases its dependent
+// early (griddepcontrol.launch_dependents): measured on a 36-layer chain, an early release let
+// the next KQKV grid occupy the SMs while this chain's small kernels still ran, and the step got
+// ~7% slower.
 #include <cuda_fp16.h>
 
 #include "m4b_internal.h"

@@ -46,6 +46,10 @@ cudaError_t launch_kqkv_partials(const KqkvLaunch& a, cudaStream_t stream);
 cudaError_t launch_kqkv_combine(const float* part, int S, float* out, int64_t out_head_stride,
                                 uint32_t flags, cudaStream_t stream);
 
+// Merge S partial records into one unnormalised record per head ([32][kPartStride]).
+cudaError_t launch_kqkv_merge_records(const float* part, int S, float* out_records, uint32_t flags,
+                                      cudaStream_t stream);
+
 // q_abs[h][r] = W_UK[h][r][:] . f16(q[h][:128]); W_UK contiguous f16 [32][512][128].
 cudaError_t launch_wkb_f16(const void* w, const float* q, int64_t q_head_stride, float* out,
                            int64_t out_head_stride, uint32_t flags, cudaStream_t stream);

@@ -456,8 +456,12 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
 // memory at the end.  S may exceed one GPU's split count (records gathered from other GPUs).
 constexpr int CMB_THREADS = 256;
 
+// record_out == 0: out[h * out_hs + d] = merged, normalised attention.
+// record_out != 0: out is a record array [32][kPartStride]: the merged, unnormalised record
+// (o = sum a_s o_s, m = m*, l = sum a_s l_s) -- the form that is exchanged between GPUs.
 __global__ void __launch_bounds__(CMB_THREADS)
-kqkv_combine_kernel(const float* __restrict__ part, int S, float* __restrict__ out, int64_t out_hs) {
+kqkv_combine_kernel(const float* __restrict__ part, int S, float* __restrict__ out, int64_t out_hs,
+                    int record_out) {
     extern __shared__ float s_alpha[];   // [S]
     __shared__ float s_red[CMB_THREADS / 32][128];
     __shared__ float s_m[CMB_THREADS / 32], s_l[CMB_THREADS / 32];
@@ -510,7 +514,18 @@ kqkv_combine_kernel(const float* __restrict__ part, int S, float* __restrict__ o
             o += s_red[w][tid];
             l += s_l[w];
         }
-        out[h * out_hs + d0 + tid] = (mstar > -INFINITY) ? o / l : 0.0f;
+        if (record_out) {
+            float* rec = out + static_cast<size_t>(h) * kPartStride;
+            rec[d0 + tid] = o;
+            if (blockIdx.y == 0 && tid == 0) {
+                rec[kPartM] = mstar;
+                rec[kPartL] = l;
+                rec[kPartL + 1] = 0.0f;
+                rec[kPartL + 2] = 0.0f;
+            }
+        } else {
+            out[h * out_hs + d0 + tid] = (mstar > -INFINITY) ? o / l : 0.0f;
+        }
     }
 }
 
@@ -559,7 +574,15 @@ cudaError_t launch_kqkv_combine(const float* part, int S, float* out, int64_t ou
     const size_t smem = static_cast<size_t>(S) * sizeof(float);
     if (smem > 48 * 1024) return cudaErrorInvalidValue;   // > 12288 records: not a real config
     return launch(kq::kqkv_combine_kernel, dim3(kHeads, kLatent / 128), dim3(kq::CMB_THREADS), smem,
-                  stream, flags, part, S, out, out_hs);
+                  stream, flags, part, S, out, out_hs, 0);
+}
+
+cudaError_t launch_kqkv_merge_records(const float* part, int S, float* out_records, uint32_t flags,
+                                      cudaStream_t stream) {
+    const size_t smem = static_cast<size_t>(S) * sizeof(float);
+    if (smem > 48 * 1024) return cudaErrorInvalidValue;
+    return launch(kq::kqkv_combine_kernel, dim3(kHeads, kLatent / 128), dim3(kq::CMB_THREADS), smem,
+                  stream, flags, part, S, out_records, static_cast<int64_t>(kPartStride), 1);
 }
 
 }  // namespace m4b

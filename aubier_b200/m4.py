@@ -38,7 +38,7 @@ FLAG_PDL, FLAG_KV_STATIC = 1, 2
 OK, EINVAL, ESCRATCH, ECUDA, EDEVICE, ENOTSUP, ETIMEOUT = range(7)
 
 OP_WKB, OP_KQKV, OP_PHASE = 0, 1, 2
-PHASE_KVWRITE, PHASE_WVB, PHASE_COMBINE_WVB = 0, 1, 2
+PHASE_KVWRITE, PHASE_WVB, PHASE_COMBINE_WVB, PHASE_MERGE = 0, 1, 2, 3
 
 
 class Tensor(ctypes.Structure):
@@ -284,6 +284,18 @@ def phase_combine_wvb(w_uv: torch.Tensor, partials: torch.Tensor,
             gtensor(partials, [PART_STRIDE, HEADS, partials.shape[0], 1]),
             _heads_desc(attn_out, LATENT) if attn_out is not None else None]
     _phase(PHASE_COMBINE_WVB, srcs, _heads_desc(out, VHEAD), flags, scratch)
+    return out
+
+
+def phase_merge_records(partials: torch.Tensor, out: torch.Tensor | None = None,
+                        flags: int = 0) -> torch.Tensor:
+    """GGML_OP_M4_PHASE selector 3 (additive): merge (S, 32, 516) partial records into one
+    unnormalised record per head, (1, 32, 516) -- the payload of the multi-GPU exchange."""
+    _need_cuda("GGML_OP_M4_PHASE", partials, out)
+    if out is None:
+        out = torch.empty(1, HEADS, PART_STRIDE, device=partials.device, dtype=torch.float32)
+    srcs = [None, gtensor(partials, [PART_STRIDE, HEADS, partials.shape[0], 1])]
+    _phase(PHASE_MERGE, srcs, gtensor(out, [PART_STRIDE, HEADS, 1, 1]), flags)
     return out
 
 

@@ -6,7 +6,8 @@ layers, each with its own seeded W_UK / W_UV / cache; 32 heads, q_nope 128, rope
 V head 128, kq_scale 1/sqrt(192).  One step = the 36 layer-steps WKB -> KQKV -> PHASE(combine +
 W_UV), captured in one CUDA graph.  With N GPUs the 262,144 keys of every layer are split into N
 contiguous slabs (strong scaling); each rank computes split-K partials over its slab and the
-partials are all-gathered over NCCL before the combine + W_UV.
+each rank's partials are merged into one record per head (66 KB), all-gathered over NCCL, and
+merged again with W_UV applied.
 
 Printed JSON line (rank 0): value = layer-steps/s of the whole job, timed on the device (max over
 ranks) around exactly --steps graph replays; e2e = the same metric with the step's queries copied
@@ -205,7 +206,8 @@ def run_ours(args, rank: int, world: int) -> None:
         qc[:, R:] = q[-1][:, NOPE:]
         qcur.append(qc)
     part = torch.empty(S, H, PART, device=dev)
-    gathered = torch.empty(world * S, H, PART, device=dev) if world > 1 else part
+    merged = torch.empty(1, H, PART, device=dev)                 # this rank's record per head
+    gathered = torch.empty(world, H, PART, device=dev) if world > 1 else part
     attn = torch.empty(H, R, device=dev)
     out = torch.empty(L, H, V, device=dev)
     flags = m4.FLAG_PDL
@@ -217,8 +219,9 @@ def run_ours(args, rank: int, world: int) -> None:
             m4.wkb(wuk[layer], q[layer][:, :NOPE], out=qcur[layer][:, :R], flags=flags)
             m4.kqkv_partials(kc[layer], qcur[layer], None, SCALE, out=part,
                              flags=flags | m4.FLAG_KV_STATIC)
-            if world > 1:
-                dist.all_gather_into_tensor(gathered, part)
+            if world > 1:   # merge the local splits, exchange one 66 KB record set per rank
+                m4.phase_merge_records(part, out=merged, flags=flags)
+                dist.all_gather_into_tensor(gathered, merged)
             m4.phase_combine_wvb(wuv[layer], gathered, out=out[layer], attn_out=attn, flags=flags)
 
     def barrier():
@@ -346,7 +349,7 @@ def run_ours(args, rank: int, world: int) -> None:
         "cpu_baseline": cpu_baseline,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": L * H * DQ * 4,
                 "d2h_bytes_per_step": L * H * V * 4},
-        "gpu_launches": 4 * L * args.steps,
+        "gpu_launches": (4 + (1 if world > 1 else 0)) * L * args.steps,
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
@@ -366,6 +369,7 @@ def main():
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    os.environ["NCCL_DEBUG"] = "WARN"          # keep rank 0's stdout to the one JSON line
     if args.impl == "reference":
         run_reference(args, rank)
         return

@@ -159,6 +159,10 @@ M4B_API int m4b_kqkv_static_scratch(const m4b_kqkv_args * args, m4b_stream_t str
  *                       from several GPUs); dst F32 [128, 1, 32]; optional src2 F32
  *                       [512, 1, 32] receives the merged attention output.  Needs scratch
  *                       >= m4b_phase_scratch_bytes(2) unless src2 is given.
+ *   phase 3  MERGE      (additive selector): src1 partial records F32 [516, 32, S]; dst F32
+ *                       [516, 32, 1]: one unnormalised record per head (o = sum a_s o_s,
+ *                       m = max m_s, l = sum a_s l_s, a_s = 2^(m_s - m)) -- what one GPU sends to
+ *                       the others in the KV-slab exchange; phase 2 merges the gathered records.
  * op_params follow ggml.c:3464-3468 (an int32 array): [0] phase, [1..6] rope f32, [7] eps,
  * [8] n_dims, [9] n_ctx_orig.
  */

@@ -74,6 +74,10 @@ def test_supports_op_accepts_the_baseline_contract():
     assert m4.supports_op(m4.OP_KQKV, [KC, QCUR], ATTN)              # mask optional
     assert m4.supports_op(m4.OP_PHASE, [WUV, ATTN], OUT, [1] + [0] * 15)
     assert m4.supports_op(m4.OP_PHASE, [WUV, PARTS], OUT, [2] + [0] * 15)
+    assert m4.supports_op(m4.OP_PHASE, [WUV, PARTS], contiguous(m4.F32, [516, 32, 1, 1], 4),
+                          [3] + [0] * 15)
+    assert not m4.supports_op(m4.OP_PHASE, [WUV, PARTS], contiguous(m4.F32, [516, 32, 2, 1], 4),
+                              [3] + [0] * 15)
 
 
 def test_supports_op_rejects_contract_violations():

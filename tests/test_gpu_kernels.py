@@ -182,6 +182,33 @@ def test_combine_wvb_matches_oracle(m4):
     assert np.array_equal(out, out2)
 
 
+def test_merge_records_two_level_equals_direct(m4):
+    """PHASE selector 3 (the multi-GPU exchange payload): merging groups of partial records into
+    one record each, then merging those, equals merging all records at once."""
+    N = 30000
+    q, w_uk, kc, w_uv = make_layer(42, N)
+    qcur = dev(qcur_of(q, w_uk))
+    mask = window_mask(N, 1000, 20000)          # some splits fully masked
+    part = m4.kqkv_partials(dev(kc), qcur, dev(mask), SCALE, splits=148)
+    groups = [part[:50], part[50:51], part[51:]]   # uneven "ranks"
+    merged = torch.cat([m4.phase_merge_records(g) for g in groups])
+    wuv = dev(w_uv)
+    a1, a2 = torch.empty(G.H, G.R, device="cuda"), torch.empty(G.H, G.R, device="cuda")
+    o1 = host(m4.phase_combine_wvb(wuv, part, attn_out=a1))
+    o2 = host(m4.phase_combine_wvb(wuv, merged, attn_out=a2))
+    assert rel_to_max(host(a2), host(a1)) <= 1e-5
+    assert rel_to_max(o2, o1) <= 1e-4
+    ref = O.kqkv(kc, qcur_of(q, w_uk), mask, SCALE, G.R)
+    assert rel_to_max(host(a2), ref) <= ATTN_TOL
+    # a record set where one group is fully masked merges to m = -inf, l = 0 and is ignored
+    empty = m4.phase_merge_records(m4.kqkv_partials(dev(kc[:300]), qcur, dev(np.full(300, -np.inf, np.float32)), SCALE))
+    e = host(empty)
+    assert np.all(e[0, :, G.R] == -np.inf) and not e[0, :, G.R + 1].any()
+    a3 = torch.empty(G.H, G.R, device="cuda")
+    m4.phase_combine_wvb(wuv, torch.cat([merged, empty]), attn_out=a3)
+    assert rel_to_max(host(a3), host(a2)) <= 1e-6
+
+
 def test_phase_wvb_matches_oracle(m4):
     _, _, _, w_uv = make_layer(51, 1)
     x = normal(5151, G.H * G.R).astype(np.float32).reshape(G.H, G.R)
