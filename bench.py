@@ -322,6 +322,7 @@ def run_ours(args, rank: int, world: int) -> None:
     if rank != 0:
         return
     cpu_baseline = None
+    _restore_stdout()
     if world == 1 and not args.no_cpu_baseline:
         try:
             cb = cpu_reference(N, reps=args.cpu_reps)
@@ -355,6 +356,27 @@ def run_ours(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+_SAVED_STDOUT = None
+
+
+def _redirect_stdout():
+    """Libraries (torch's NCCL process group, NCCL) print banners on fd 1; the contract is one JSON
+    line on rank 0's stdout, so fd 1 points at stderr until that line is printed."""
+    global _SAVED_STDOUT
+    sys.stdout.flush()
+    _SAVED_STDOUT = os.dup(1)
+    os.dup2(2, 1)
+
+
+def _restore_stdout():
+    global _SAVED_STDOUT
+    if _SAVED_STDOUT is not None:
+        sys.stdout.flush()
+        os.dup2(_SAVED_STDOUT, 1)
+        os.close(_SAVED_STDOUT)
+        _SAVED_STDOUT = None
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -369,10 +391,10 @@ def main():
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
-    os.environ["NCCL_DEBUG"] = "WARN"          # keep rank 0's stdout to the one JSON line
     if args.impl == "reference":
         run_reference(args, rank)
         return
+    _redirect_stdout()
     import datetime
 
     import torch
