@@ -1,0 +1,389 @@
+// m4b_exchange.cu -- the KV-slab exchange between GPUs, fused into the merge kernels over NVLink.
+//
+// Long contexts are split into contiguous KV slabs, one per GPU (one process per GPU).  Each GPU
+// computes split-K partial records over its slab; the only data that must cross GPUs is one
+// merged record per head (32 x 516 values).  Instead of a library collective, the kernel that
+// merges this GPU's splits stores its record straight into every peer's receive buffer through
+// CUDA IPC peer mappings (NVLink / NVSwitch), and the kernel that consumes the records polls its
+// own memory.  No multicast and no TMA reads of peer memory are used.
+//
+// Flag-in-word records.  Every value travels as one 8-byte word {f32 value, u32 epoch} written
+// with a single 64-bit store, so a reader that sees the current epoch in a word also sees that
+// word's value: no memory fence, no separate flag and no second NVLink trip.  The cost is 8 bytes
+// per 4-byte value, 132 KB per rank and exchange.
+//
+// Per-GPU buffer (allocated once at set-up, shared by IPC handle):
+//   recv[2][world][32][516] u64   records {value, epoch}, double-buffered by epoch parity
+//   epoch u64                     exchanges published by this GPU so far
+//   arrive u32                    CTA arrival counter of the publishing kernel
+// Every value that changes per call (the epoch, the buffer parity) is read from device memory, so
+// both kernels can be captured once in a CUDA graph and replayed.
+//
+// Reuse of a parity half is safe: a GPU publishes epoch e+2 only after its own consumer of epoch
+// e+1 saw every peer's e+1 record, which every peer published after consuming epoch e.
+#include <cstring>
+
+#include "m4b_internal.h"
+#include "m4b_ptx.cuh"
+
+struct m4b_exchange {
+    int world;
+    int rank;
+    int device;
+    char* local;                         // this GPU's buffer
+    char* peer[m4b::kMaxWorld];          // every rank's buffer as mapped here (peer[rank] = local)
+    bool opened[m4b::kMaxWorld];
+    size_t bytes;
+};
+
+namespace m4b {
+namespace xch {
+
+constexpr size_t kRecordWords = static_cast<size_t>(kHeads) * kPartStride;
+
+struct Layout {
+    size_t recv_off, epoch_off, arrive_off, bytes;
+};
+
+inline Layout layout(int world) {
+    Layout l;
+    l.recv_off = 0;
+    l.epoch_off = 2 * static_cast<size_t>(world) * kRecordWords * sizeof(uint64_t);
+    l.arrive_off = l.epoch_off + sizeof(uint64_t);
+    l.bytes = (l.arrive_off + 256 + 255) & ~static_cast<size_t>(255);
+    return l;
+}
+
+struct PeerPtrs {
+    char* p[kMaxWorld];
+};
+
+__device__ __forceinline__ uint64_t* record(char* base, const Layout& L, uint64_t e, int world,
+                                            int r, int h) {
+    return reinterpret_cast<uint64_t*>(base + L.recv_off) +
+           ((e & 1) * world + r) * kRecordWords + static_cast<size_t>(h) * kPartStride;
+}
+
+__device__ __forceinline__ void st_word(uint64_t* a, float v, uint32_t e) {
+    const uint64_t w = (static_cast<uint64_t>(e) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(w) : "memory");
+}
+
+// Poll one word until it carries epoch e; bounded: after M4B_WAIT_LIMIT_CYCLES (counted from t0)
+// the device status becomes TIMEOUT and whatever the word holds is returned.
+__device__ __forceinline__ float ld_word(const uint64_t* a, uint32_t e, long long t0) {
+    uint64_t w;
+    for (;;) {
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(a) : "memory");
+        if (static_cast<uint32_t>(w >> 32) == e) break;
+        if (clock64() - t0 > M4B_WAIT_LIMIT_CYCLES) {
+            atomicExch(&g_status, DEV_STATUS_TIMEOUT);
+            break;
+        }
+    }
+    return __uint_as_float(static_cast<uint32_t>(w));
+}
+
+constexpr int THREADS = 256;
+
+// Merge this GPU's S split records (m4-kqkv.cu:318-338 rule, log2 units) into one unnormalised
+// record per head and store it, epoch-tagged, into slot [rank] of every peer's receive buffer.
+// grid (32 heads, 4 blocks of 128 latent columns).
+__global__ void __launch_bounds__(THREADS)
+publish_kernel(const float* __restrict__ part, int S, PeerPtrs peers, char* local, int world,
+               int rank, Layout L) {
+    extern __shared__ float s_alpha[];   // [S]
+    __shared__ float s_red[THREADS / 32][128];
+    __shared__ float s_m[THREADS / 32], s_l[THREADS / 32];
+    pdl_wait();
+    const int h = blockIdx.x;
+    const int d0 = blockIdx.y * 128;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t ss = static_cast<size_t>(kHeads) * kPartStride;
+    const float* ph = part + static_cast<size_t>(h) * kPartStride;
+    const uint64_t e = *reinterpret_cast<volatile uint64_t*>(local + L.epoch_off) + 1;
+
+    float m = -INFINITY;
+    for (int s = tid; s < S; s += THREADS) m = fmaxf(m, __ldg(ph + s * ss + kPartM));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (lane == 0) s_m[warp] = m;
+    __syncthreads();
+    float mstar = s_m[0];
+#pragma unroll
+    for (int w = 1; w < THREADS / 32; ++w) mstar = fmaxf(mstar, s_m[w]);
+    float lsum = 0.0f;
+    for (int s = tid; s < S; s += THREADS) {
+        const float ms = __ldg(ph + s * ss + kPartM);
+        const float a = (ms > -INFINITY) ? exp2f(ms - mstar) : 0.0f;
+        s_alpha[s] = a;
+        lsum += a * __ldg(ph + s * ss + kPartL);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
+    if (lane == 0) s_l[warp] = lsum;
+    __syncthreads();
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* col = ph + d0 + 4 * lane;
+#pragma unroll 4
+    for (int s = warp; s < S; s += THREADS / 32) {
+        const float a = s_alpha[s];
+        const float4 v = __ldg(reinterpret_cast<const float4*>(col + s * ss));
+        acc.x = fmaf(a, v.x, acc.x);
+        acc.y = fmaf(a, v.y, acc.y);
+        acc.z = fmaf(a, v.z, acc.z);
+        acc.w = fmaf(a, v.w, acc.w);
+    }
+    *reinterpret_cast<float4*>(&s_red[warp][4 * lane]) = acc;
+    __syncthreads();
+    const uint32_t e32 = static_cast<uint32_t>(e);
+    if (tid < 128) {
+        float o = 0.0f, l = 0.0f;
+#pragma unroll
+        for (int w = 0; w < THREADS / 32; ++w) {
+            o += s_red[w][tid];
+            l += s_l[w];
+        }
+#pragma unroll
+        for (int p = 0; p < kMaxWorld; ++p) {   // unrolled: the peer table stays in registers
+            if (p >= world) break;
+            uint64_t* rec = record(peers.p[p], L, e, world, rank, h);
+            st_word(rec + d0 + tid, o, e32);
+            if (blockIdx.y == 0 && tid == 0) {
+                st_word(rec + kPartM, mstar, e32);
+                st_word(rec + kPartL, l, e32);
+            }
+        }
+    }
+    // The epoch advances once every CTA has read it (local bookkeeping; the next kernels on this
+    // GPU are ordered after this one by the stream).
+    __syncthreads();
+    if (tid == 0) {
+        unsigned* arrive = reinterpret_cast<unsigned*>(local + L.arrive_off);
+        if (atomicAdd(arrive, 1u) == gridDim.x * gridDim.y - 1) {
+            *arrive = 0;
+            *reinterpret_cast<volatile uint64_t*>(local + L.epoch_off) = e;
+        }
+    }
+}
+
+// Wait for every rank's record of head h (polling the epoch in each word), merge the `world`
+// records, normalise, then apply W_UV to the merged head:
+//   out[h][j] = sum_r W_UV[h][j][r] * f16(attn[h][r])          (m4-phase.cu:52-89, ggml F16 mul_mat)
+// grid (32 heads, 8 blocks of 16 W_UV rows); each CTA merges its head's 512 columns itself (an L2
+// read of world x 4 KB) so the gemv needs no second launch.  The CTA of row block 0 also writes
+// the normalised attention row when attn_out is given.
+constexpr int GW_ROWS_PER_WARP = 2;
+constexpr int GW_ROWS = GW_ROWS_PER_WARP * (THREADS / 32);   // 16 rows per CTA
+
+__global__ void __launch_bounds__(THREADS)
+gather_wvb_kernel(char* __restrict__ local, int world, Layout L, const __half* __restrict__ w_uv,
+                  float* __restrict__ attn_out, int64_t attn_hs, float* __restrict__ out,
+                  int64_t out_hs) {
+    __shared__ float s_m[kMaxWorld], s_l[kMaxWorld];
+    __shared__ __align__(16) float s_x[kLatent];
+    const int h = blockIdx.x;
+    const int j0 = blockIdx.y * GW_ROWS;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    // W_UV rows first: they do not depend on any earlier kernel
+    uint4 wv[GW_ROWS_PER_WARP][2];
+#pragma unroll
+    for (int it = 0; it < GW_ROWS_PER_WARP; ++it)
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+            wv[it][u] = gemv::ldg_stream(w_uv + (static_cast<size_t>(h) * kVHead + j0 +
+                                                 warp * GW_ROWS_PER_WARP + it) * kLatent +
+                                         256 * u + 8 * lane);
+    pdl_wait();
+    const uint64_t e = *reinterpret_cast<volatile uint64_t*>(local + L.epoch_off);
+    const uint32_t e32 = static_cast<uint32_t>(e);
+    const long long t0 = clock64();
+    if (tid < world) {
+        const uint64_t* rec = record(local, L, e, world, tid, h);
+        s_m[tid] = ld_word(rec + kPartM, e32, t0);
+        s_l[tid] = ld_word(rec + kPartL, e32, t0);
+    }
+    float v[2][kMaxWorld];
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; ++r) {
+        if (r < world) {
+            const uint64_t* rec = record(local, L, e, world, r, h);
+            v[0][r] = ld_word(rec + tid, e32, t0);
+            v[1][r] = ld_word(rec + tid + THREADS, e32, t0);
+        }
+    }
+    __syncthreads();
+    float mstar = -INFINITY;
+    for (int r = 0; r < world; ++r) mstar = fmaxf(mstar, s_m[r]);
+    float l = 0.0f, o0 = 0.0f, o1 = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; ++r) {
+        if (r < world) {
+            const float a = (s_m[r] > -INFINITY) ? exp2f(s_m[r] - mstar) : 0.0f;
+            l = fmaf(a, s_l[r], l);
+            o0 = fmaf(a, v[0][r], o0);
+            o1 = fmaf(a, v[1][r], o1);
+        }
+    }
+    const float inv = (mstar > -INFINITY && l > 0.0f) ? 1.0f / l : 0.0f;
+    const float x0 = (inv != 0.0f) ? o0 * inv : 0.0f;
+    const float x1 = (inv != 0.0f) ? o1 * inv : 0.0f;
+    if (attn_out != nullptr && blockIdx.y == 0) {
+        attn_out[h * attn_hs + tid] = x0;
+        attn_out[h * attn_hs + tid + THREADS] = x1;
+    }
+    s_x[tid] = gemv::round_f16(x0);
+    s_x[tid + THREADS] = gemv::round_f16(x1);
+    __syncthreads();
+    float xf[2][8];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const float4 a = *reinterpret_cast<const float4*>(&s_x[256 * u + 8 * lane]);
+        const float4 b = *reinterpret_cast<const float4*>(&s_x[256 * u + 8 * lane + 4]);
+        xf[u][0] = a.x; xf[u][1] = a.y; xf[u][2] = a.z; xf[u][3] = a.w;
+        xf[u][4] = b.x; xf[u][5] = b.y; xf[u][6] = b.z; xf[u][7] = b.w;
+    }
+#pragma unroll
+    for (int it = 0; it < GW_ROWS_PER_WARP; ++it) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            float wf[8];
+            gemv::unpack8(wv[it][u], wf);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc = fmaf(wf[j], xf[u][j], acc);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        if (lane == 0) out[h * out_hs + j0 + warp * GW_ROWS_PER_WARP + it] = acc;
+    }
+}
+
+}  // namespace xch
+}  // namespace m4b
+
+using namespace m4b;
+
+extern "C" {
+
+M4B_API int m4b_exchange_create(int world, int rank, m4b_exchange** out) {
+    if (!out || world < 1 || world > kMaxWorld || rank < 0 || rank >= world) return M4B_EINVAL;
+    *out = nullptr;
+    int rc = device_check(nullptr);
+    if (rc != M4B_OK) return rc;
+    m4b_exchange* x = new m4b_exchange();
+    std::memset(x, 0, sizeof(*x));
+    x->world = world;
+    x->rank = rank;
+    if (cudaGetDevice(&x->device) != cudaSuccess) {
+        delete x;
+        return M4B_ECUDA;
+    }
+    const xch::Layout L = xch::layout(world);
+    x->bytes = L.bytes;
+    void* p = nullptr;
+    if (cudaMalloc(&p, L.bytes) != cudaSuccess) {   // set-up time, not on the op path
+        delete x;
+        return M4B_ECUDA;
+    }
+    if (cudaMemset(p, 0, L.bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        cudaFree(p);
+        delete x;
+        return M4B_ECUDA;
+    }
+    x->local = static_cast<char*>(p);
+    x->peer[rank] = x->local;
+    *out = x;
+    return M4B_OK;
+}
+
+M4B_API int m4b_exchange_ipc_handle(const m4b_exchange* x, void* handle_out) {
+    if (!x || !handle_out) return M4B_EINVAL;
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, x->local) != cudaSuccess) return M4B_ECUDA;
+    std::memcpy(handle_out, &h, sizeof(h));
+    return M4B_OK;
+}
+
+M4B_API int m4b_exchange_open(m4b_exchange* x, const void* handles) {
+    if (!x || !handles) return M4B_EINVAL;
+    const char* hs = static_cast<const char*>(handles);
+    for (int r = 0; r < x->world; ++r) {
+        if (r == x->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, hs + static_cast<size_t>(r) * M4B_IPC_HANDLE_BYTES, sizeof(h));
+        void* p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+            return M4B_ECUDA;
+        x->peer[r] = static_cast<char*>(p);
+        x->opened[r] = true;
+    }
+    return M4B_OK;
+}
+
+M4B_API int m4b_exchange_detach(m4b_exchange* x) {
+    if (!x) return M4B_OK;
+    int rc = M4B_OK;
+    if (cudaDeviceSynchronize() != cudaSuccess) rc = M4B_ECUDA;   // no launch may still use a peer
+    for (int r = 0; r < x->world; ++r) {
+        if (x->opened[r] && cudaIpcCloseMemHandle(x->peer[r]) != cudaSuccess) rc = M4B_ECUDA;
+        if (r != x->rank) x->peer[r] = nullptr;
+        x->opened[r] = false;
+    }
+    return rc;
+}
+
+M4B_API int m4b_exchange_destroy(m4b_exchange* x) {
+    if (!x) return M4B_OK;
+    int rc = m4b_exchange_detach(x);   // no-op when the caller detached already
+    if (x->local && cudaFree(x->local) != cudaSuccess) rc = M4B_ECUDA;
+    delete x;
+    return rc;
+}
+
+M4B_API int m4b_exchange_publish(m4b_exchange* x, const m4b_phase_args* a, m4b_stream_t stream) {
+    if (!x || !a) return M4B_EINVAL;
+    for (int r = 0; r < x->world; ++r)
+        if (!x->peer[r]) return M4B_EINVAL;   // m4b_exchange_open not done
+    int rc = check_partials(a->src[1], 0);
+    if (rc != M4B_OK) return rc;
+    rc = device_check(nullptr);
+    if (rc != M4B_OK) return rc;
+    xch::PeerPtrs pp;
+    for (int r = 0; r < kMaxWorld; ++r) pp.p[r] = r < x->world ? x->peer[r] : nullptr;
+    const int S = static_cast<int>(a->src[1].ne[2]);
+    const size_t smem = static_cast<size_t>(S) * sizeof(float);
+    if (smem > 48 * 1024) return M4B_EINVAL;
+    return status_of(launch(xch::publish_kernel, dim3(kHeads, kLatent / 128), dim3(xch::THREADS),
+                            smem, reinterpret_cast<cudaStream_t>(stream), a->flags,
+                            static_cast<const float*>(a->src[1].data), S, pp, x->local, x->world, x->rank,
+                            xch::layout(x->world)));
+}
+
+M4B_API int m4b_exchange_combine_wvb(m4b_exchange* x, const m4b_phase_args* a,
+                                     m4b_stream_t stream) {
+    if (!x || !a) return M4B_EINVAL;
+    if (!x->local) return M4B_EINVAL;
+    int rc = check_wuv(a->src[0]);
+    if (rc != M4B_OK) return rc;
+    rc = check_phase_dst(a->dst);
+    if (rc != M4B_OK) return rc;
+    float* attn = nullptr;
+    int64_t attn_hs = kLatent;
+    if (a->src[2].data != nullptr) {
+        if (check_attn(a->src[2]) != M4B_OK) return M4B_EINVAL;
+        attn = static_cast<float*>(a->src[2].data);
+        attn_hs = static_cast<int64_t>(a->src[2].nb[2] / 4);
+    }
+    rc = device_check(nullptr);
+    if (rc != M4B_OK) return rc;
+    return status_of(launch(xch::gather_wvb_kernel, dim3(kHeads, kVHead / xch::GW_ROWS),
+                            dim3(xch::THREADS), 0, reinterpret_cast<cudaStream_t>(stream), a->flags,
+                            x->local, x->world, xch::layout(x->world),
+                            static_cast<const __half*>(a->src[0].data), attn, attn_hs,
+                            static_cast<float*>(a->dst.data),
+                            static_cast<int64_t>(a->dst.nb[2] / 4)));
+}
+
+}  // extern "C"

@@ -26,6 +26,7 @@ constexpr int kPartL = kLatent + 1;
 
 constexpr int kTileKeys = 128;   // keys per KQKV tile (the tcgen05 MMA M dimension)
 constexpr int kMaxSplits = 148;  // one persistent CTA per B200 SM
+constexpr int kMaxWorld = 8;     // GPUs of one node in the KV-slab exchange
 
 struct KqkvLaunch {
     const void* kcache;

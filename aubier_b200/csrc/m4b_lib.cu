@@ -5,3 +5,4 @@
 #include "m4b_gemv.cu"
 #include "m4b_api.cu"
 #include "m4b_noalloc.cu"
+#include "m4b_exchange.cu"

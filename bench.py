@@ -208,6 +208,12 @@ def run_ours(args, rank: int, world: int) -> None:
     part = torch.empty(S, H, PART, device=dev)
     merged = torch.empty(1, H, PART, device=dev)                 # this rank's record per head
     gathered = torch.empty(world, H, PART, device=dev) if world > 1 else part
+    xchg = None
+    if world > 1 and args.exchange == "p2p":
+        from aubier_b200.exchange import PeerExchange
+        xchg = PeerExchange(world, rank)
+        torch.cuda.synchronize()            # every rank's inputs exist before the first exchange
+        dist.barrier()
     attn = torch.empty(H, R, device=dev)
     out = torch.empty(L, H, V, device=dev)
     flags = m4.FLAG_PDL
@@ -219,7 +225,11 @@ def run_ours(args, rank: int, world: int) -> None:
             m4.wkb(wuk[layer], q[layer][:, :NOPE], out=qcur[layer][:, :R], flags=flags)
             m4.kqkv_partials(kc[layer], qcur[layer], None, SCALE, out=part,
                              flags=flags | m4.FLAG_KV_STATIC)
-            if world > 1:   # merge the local splits, exchange one 66 KB record set per rank
+            if xchg is not None:   # fused: merge + NVLink stores into every peer, then wait+merge
+                xchg.publish(part, flags=flags)
+                xchg.combine_wvb(wuv[layer], out=out[layer], attn_out=attn, flags=flags)
+                continue
+            if world > 1:   # library collective: merge the local splits, all-gather 66 KB per rank
                 m4.phase_merge_records(part, out=merged, flags=flags)
                 dist.all_gather_into_tensor(gathered, merged)
             m4.phase_combine_wvb(wuv[layer], gathered, out=out[layer], attn_out=attn, flags=flags)
@@ -318,6 +328,8 @@ def run_ours(args, rank: int, world: int) -> None:
 
     assert m4.device_status() == m4.OK
     del graph, graph_e2e, graph_kq           # release graphs before the process group
+    if xchg is not None:
+        xchg.close()                         # collective: detach, meet, free
 
     if rank != 0:
         return
@@ -338,7 +350,10 @@ def run_ours(args, rank: int, world: int) -> None:
         "config": {"workload": "BASELINE config 4: 1 decode token, 262144-key f16 latent+rope KV "
                                "cache, 36 layers, 32 heads, nope 128 / rope 64 / latent 512 / V 128",
                    "keys": N, "layers": L, "keys_per_gpu": n_loc, "splits_per_gpu": S,
-                   "parallelism": f"kv-slab x{world}" + (" + nccl all-gather" if world > 1 else ""),
+                   "parallelism": f"kv-slab x{world}" + (
+                       "" if world == 1 else
+                       " + fused NVLink record exchange" if args.exchange == "p2p" else
+                       " + nccl all-gather of merged records"),
                    "l2": "inputs larger than L2 (36 layers x 302 MB KV per step)",
                    "step": "WKB -> KQKV split-K partials -> PHASE combine+W_UV per layer, "
                            "one CUDA graph per step"},
@@ -350,7 +365,8 @@ def run_ours(args, rank: int, world: int) -> None:
         "cpu_baseline": cpu_baseline,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": L * H * DQ * 4,
                 "d2h_bytes_per_step": L * H * V * 4},
-        "gpu_launches": (4 + (1 if world > 1 else 0)) * L * args.steps,
+        "gpu_launches": (4 + (1 if world > 1 else 0)) * L * args.steps,   # p2p: publish+gather
+                                                                             # replace merge+combine
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
@@ -387,6 +403,8 @@ def main():
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--cpu-reps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="N>1: fused NVLink exchange in the merge kernels, or NCCL all-gather")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -177,6 +177,39 @@ typedef struct m4b_phase_args {
 
 M4B_API int m4b_phase(const m4b_phase_args * args, m4b_stream_t stream);
 
+/*
+ * The KV-slab exchange between the GPUs of one node, fused into the merge kernels (no counterpart
+ * in the reference, which runs on one GPU: engine/m1_engine.cpp:2165).  One process per GPU; each
+ * GPU computes split-K records over its slab of the cache (m4b_kqkv_partials), then
+ *   m4b_exchange_publish     merges them into one record per head and stores that record into
+ *                            every peer's receive buffer over NVLink (CUDA IPC mappings), each
+ *                            value tagged with the exchange's epoch; src[1] = records [516, 32, S]
+ *   m4b_exchange_combine_wvb waits (bounded) until every GPU's record of the current exchange has
+ *                            arrived, merges them and applies W_UV, in one kernel: src[0] = W_UV,
+ *                            dst = F32 [128, 1, 32]; the optional src[2] (F32 [512, 1, 32])
+ *                            receives the merged attention.  No scratch.
+ * Set-up (not capture-safe, once per process): m4b_exchange_create allocates this GPU's buffer;
+ * exchange the M4B_IPC_HANDLE_BYTES handles of all ranks (m4b_exchange_ipc_handle) through any
+ * host channel, then m4b_exchange_open with all of them, rank-ordered.  The two launch entry
+ * points are plain launches (capturable); every GPU must call them the same number of times.
+ * A peer that never publishes makes the combine give up after ~1 s and report M4B_ETIMEOUT through
+ * m4b_device_status(); the output of that call is undefined.
+ * Tear-down: every rank calls m4b_exchange_detach (unmaps the peers' buffers), then all ranks meet
+ * on the host, then each calls m4b_exchange_destroy (frees its own buffer) -- an exporting process
+ * must not free a buffer that another process still has mapped.
+ */
+#define M4B_IPC_HANDLE_BYTES 64
+typedef struct m4b_exchange m4b_exchange;
+
+M4B_API int m4b_exchange_create(int world, int rank, m4b_exchange ** out);
+M4B_API int m4b_exchange_ipc_handle(const m4b_exchange * x, void * handle_out);
+M4B_API int m4b_exchange_open(m4b_exchange * x, const void * handles);
+M4B_API int m4b_exchange_detach(m4b_exchange * x);
+M4B_API int m4b_exchange_destroy(m4b_exchange * x);
+M4B_API int m4b_exchange_publish(m4b_exchange * x, const m4b_phase_args * args, m4b_stream_t stream);
+M4B_API int m4b_exchange_combine_wvb(m4b_exchange * x, const m4b_phase_args * args,
+                                     m4b_stream_t stream);
+
 /* Sizes.  geometry: 0 = BASELINE, 1 = MISTRAL_SMALL. */
 M4B_API uint64_t m4b_kqkv_scratch_bytes(int geometry, int64_t n_kv);
 M4B_API uint64_t m4b_phase_scratch_bytes(int phase);

@@ -122,6 +122,22 @@ def test_entry_points_refuse_bad_operands_before_any_cuda_call():
     assert lib.m4b_kqkv(None, None) == m4.EINVAL
 
 
+def test_exchange_refuses_bad_arguments_before_any_cuda_call():
+    from aubier_b200 import exchange  # noqa: F401  (declares the argument types)
+    lib = m4.lib()
+    h = ctypes.c_void_p()
+    for world, rank in ((0, 0), (9, 0), (2, 2), (2, -1)):
+        assert lib.m4b_exchange_create(world, rank, ctypes.byref(h)) == m4.EINVAL
+    assert lib.m4b_exchange_create(2, 0, None) == m4.EINVAL
+    assert lib.m4b_exchange_detach(None) == m4.OK
+    assert lib.m4b_exchange_destroy(None) == m4.OK
+    assert lib.m4b_exchange_ipc_handle(None, None) == m4.EINVAL
+    assert lib.m4b_exchange_open(None, None) == m4.EINVAL
+    p = m4.PhaseArgs()
+    assert lib.m4b_exchange_publish(None, ctypes.byref(p), None) == m4.EINVAL
+    assert lib.m4b_exchange_combine_wvb(None, ctypes.byref(p), None) == m4.EINVAL
+
+
 def test_scratch_sizes():
     assert m4.kqkv_scratch_bytes(262144) == 148 * 32 * 516 * 4
     assert m4.kqkv_scratch_bytes(4096) == 32 * 32 * 516 * 4
