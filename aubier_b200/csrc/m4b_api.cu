@@ -74,11 +74,15 @@ int check_wkb(const m4b_tensor& w, const m4b_tensor& x, const m4b_tensor& dst, i
         return M4B_ENOTSUP;
     }
     if (!type_ne(w, M4B_TYPE_F16, kNope, kLatent, kHeads, 1) || !packed3(w, 2)) return M4B_EINVAL;
-    if (!type_ne(x, M4B_TYPE_F32, kNope, kHeads, 1, 1) || x.nb[0] != 4 || x.nb[1] % 4 != 0 ||
-        x.nb[1] < 4u * kNope)
+    // ne[2] = tokens: 1 in the reference's op (ggml.c:3398-3423); up to kMaxSeqs here, for the
+    // ragged batch (token stride nb[2])
+    const int64_t nt = x.ne[2];
+    if (nt < 1 || nt > kMaxSeqs) return M4B_EINVAL;
+    if (!type_ne(x, M4B_TYPE_F32, kNope, kHeads, nt, 1) || x.nb[0] != 4 || x.nb[1] % 4 != 0 ||
+        x.nb[1] < 4u * kNope || x.nb[2] % 4 != 0)
         return M4B_EINVAL;
-    if (!type_ne(dst, M4B_TYPE_F32, kLatent, kHeads, 1, 1) || dst.nb[0] != 4 ||
-        dst.nb[1] % 4 != 0 || dst.nb[1] < 4u * kLatent)
+    if (!type_ne(dst, M4B_TYPE_F32, kLatent, kHeads, nt, 1) || dst.nb[0] != 4 ||
+        dst.nb[1] % 4 != 0 || dst.nb[1] < 4u * kLatent || dst.nb[2] % 4 != 0)
         return M4B_EINVAL;
     if (!w.data || !x.data || !dst.data || !aligned(w.data, 16) || !aligned(x.data, 4) ||
         !aligned(dst.data, 4))
@@ -132,6 +136,7 @@ int check_partials(const m4b_tensor& p, int64_t max_splits) {
 
 KqkvLaunch make_kqkv_launch(const m4b_kqkv_args& a, int splits, float* part) {
     KqkvLaunch l;
+    l.q_token_stride = 0;
     l.kcache = a.src0.data;
     l.kcache_row_bytes = a.src0.nb[1];
     l.n_kv = a.src0.ne[1];
@@ -144,6 +149,34 @@ KqkvLaunch make_kqkv_launch(const m4b_kqkv_args& a, int splits, float* part) {
     l.flags = a.flags;
     return l;
 }
+
+// Ragged batch (additive): kcache as for KQKV; q F32 [576, 32, T]; seq_base / seq_len I32 [T];
+// dst F32 [512, T, 32] (token stride nb[1], head stride nb[2]: ggml's kqv for T tokens).
+int check_kqkv_ragged(const m4b_kqkv_ragged_args& a) {
+    m4b_kqkv_args k;
+    std::memset(&k, 0, sizeof(k));
+    k.src0 = a.kcache;
+    k.kq_scale = a.kq_scale;
+    const int64_t T = a.q.ne[2];
+    if (T < 1 || T > kMaxSeqs) return M4B_EINVAL;
+    k.src1 = a.q;
+    k.src1.ne[2] = 1;   // the single-token check below covers dims 0..1
+    int rc = check_kqkv_inputs(k);
+    if (rc != M4B_OK) return rc;
+    if (a.q.ne[3] != 1 || a.q.nb[2] % 4 != 0) return M4B_EINVAL;
+    if (a.kcache.ne[1] > (int64_t(1) << 30) - kTileKeys) return M4B_EINVAL;
+    for (const m4b_tensor* t : {&a.seq_base, &a.seq_len})
+        if (!type_ne(*t, M4B_TYPE_I32, T, 1, 1, 1) || t->nb[0] != 4 || !t->data ||
+            !aligned(t->data, 4))
+            return M4B_EINVAL;
+    const m4b_tensor& d = a.dst;
+    if (!type_ne(d, M4B_TYPE_F32, kLatent, T, kHeads, 1) || d.nb[0] != 4 || d.nb[1] % 4 != 0 ||
+        d.nb[2] % 4 != 0 || !d.data || !aligned(d.data, 4))
+        return M4B_EINVAL;
+    return M4B_OK;
+}
+
+uint64_t ragged_records(int64_t n_seq) { return static_cast<uint64_t>(kMaxSplits + n_seq - 1); }
 
 // ---------------------------------------------------------------------------------------------
 // PHASE
@@ -170,6 +203,20 @@ int check_attn(const m4b_tensor& x) {   // F32 [512, 1, 32] with a head stride n
     return M4B_OK;
 }
 
+// PHASE selector 1 for T tokens: x F32 [512, T, 32], dst F32 [128, T, 32] (token stride nb[1],
+// head stride nb[2]); T = 1 is the reference's op (ggml.c:3517-3539).
+int check_wvb_tokens(const m4b_tensor& x, const m4b_tensor& d) {
+    const int64_t nt = x.ne[1];
+    if (nt < 1 || nt > kMaxSeqs) return M4B_EINVAL;
+    if (!type_ne(x, M4B_TYPE_F32, kLatent, nt, kHeads, 1) || x.nb[0] != 4 || x.nb[1] % 4 != 0 ||
+        x.nb[2] % 4 != 0 || x.nb[2] < 4u * kLatent || !x.data || !aligned(x.data, 4))
+        return M4B_EINVAL;
+    if (!type_ne(d, M4B_TYPE_F32, kVHead, nt, kHeads, 1) || d.nb[0] != 4 || d.nb[1] % 4 != 0 ||
+        d.nb[2] % 4 != 0 || d.nb[2] < 4u * kVHead || !d.data || !aligned(d.data, 4))
+        return M4B_EINVAL;
+    return M4B_OK;
+}
+
 int check_phase(const m4b_phase_args& a) {
     const int phase = a.op_params[0];
     switch (phase) {
@@ -178,9 +225,7 @@ int check_phase(const m4b_phase_args& a) {
         case 1: {
             int rc = check_wuv(a.src[0]);
             if (rc != M4B_OK) return rc;
-            rc = check_attn(a.src[1]);
-            if (rc != M4B_OK) return rc;
-            return check_phase_dst(a.dst);
+            return check_wvb_tokens(a.src[1], a.dst);
         }
         case 2: {
             int rc = check_wuv(a.src[0]);
@@ -259,10 +304,11 @@ int m4b_wkb(const m4b_wkb_args* a, m4b_stream_t stream) {
     if (rc != M4B_OK) return rc;
     rc = device_check(nullptr);
     if (rc != M4B_OK) return rc;
-    return status_of(launch_wkb_f16(a->src0.data, static_cast<const float*>(a->src1.data),
-                                    static_cast<int64_t>(a->src1.nb[1] / 4),
-                                    static_cast<float*>(a->dst.data),
-                                    static_cast<int64_t>(a->dst.nb[1] / 4), a->flags,
+    const Rows qr = {static_cast<int64_t>(a->src1.nb[1] / 4), static_cast<int64_t>(a->src1.nb[2] / 4)};
+    const Rows outr = {static_cast<int64_t>(a->dst.nb[1] / 4), static_cast<int64_t>(a->dst.nb[2] / 4)};
+    return status_of(launch_wkb_f16(a->src0.data, static_cast<const float*>(a->src1.data), qr,
+                                    static_cast<float*>(a->dst.data), outr,
+                                    static_cast<int>(a->src1.ne[2]), a->flags,
                                     reinterpret_cast<cudaStream_t>(stream)));
 }
 
@@ -300,6 +346,47 @@ int m4b_kqkv_partials(const m4b_kqkv_args* a, m4b_stream_t stream) {
         reinterpret_cast<cudaStream_t>(stream)));
 }
 
+uint64_t m4b_kqkv_ragged_scratch_bytes(int64_t n_seq) {
+    if (n_seq < 1 || n_seq > kMaxSeqs) return 0;
+    return ragged_records(n_seq) * kHeads * kPartStride * sizeof(float);
+}
+
+int m4b_kqkv_ragged(const m4b_kqkv_ragged_args* a, m4b_stream_t stream) {
+    if (!a) return M4B_EINVAL;
+    int rc = check_kqkv_ragged(*a);
+    if (rc != M4B_OK) return rc;
+    const int64_t T = a->q.ne[2];
+    if (!a->scratch || a->scratch_bytes < m4b_kqkv_ragged_scratch_bytes(T) ||
+        !aligned(a->scratch, 16))
+        return M4B_ESCRATCH;
+    int sms = 0;
+    rc = device_check(&sms);
+    if (rc != M4B_OK) return rc;
+    const int G = std::min(sms, kMaxSplits);
+    KqkvLaunch l;
+    l.kcache = a->kcache.data;
+    l.kcache_row_bytes = a->kcache.nb[1];
+    l.n_kv = a->kcache.ne[1];
+    l.q = static_cast<const float*>(a->q.data);
+    l.q_head_stride = static_cast<int64_t>(a->q.nb[1] / 4);
+    l.q_token_stride = static_cast<int64_t>(a->q.nb[2] / 4);
+    l.mask = nullptr;
+    l.kq_scale = a->kq_scale;
+    l.splits = G;
+    l.part = static_cast<float*>(a->scratch);
+    l.flags = a->flags;
+    l.seq_base = static_cast<const int32_t*>(a->seq_base.data);
+    l.seq_len = static_cast<const int32_t*>(a->seq_len.data);
+    l.n_seq = static_cast<int>(T);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = launch_kqkv_partials(l, s);
+    if (e != cudaSuccess) return M4B_ECUDA;
+    return status_of(launch_kqkv_ragged_combine(
+        l.part, l.seq_base, l.seq_len, l.n_seq, l.n_kv, G, static_cast<float*>(a->dst.data),
+        static_cast<int64_t>(a->dst.nb[2] / 4), static_cast<int64_t>(a->dst.nb[1] / 4),
+        a->flags & M4B_FLAG_PDL, s));
+}
+
 int m4b_phase(const m4b_phase_args* a, m4b_stream_t stream) {
     if (!a) return M4B_EINVAL;
     int rc = check_phase(*a);
@@ -329,8 +416,11 @@ int m4b_phase(const m4b_phase_args* a, m4b_stream_t stream) {
                                                    a->flags & M4B_FLAG_PDL, s));
     }
     if (phase == 1) {
+        const Rows xr = {static_cast<int64_t>(a->src[1].nb[2] / 4),
+                         static_cast<int64_t>(a->src[1].nb[1] / 4)};
+        const Rows outr = {out_hs, static_cast<int64_t>(a->dst.nb[1] / 4)};
         return status_of(launch_wvb_f16(a->src[0].data, static_cast<const float*>(a->src[1].data),
-                                        static_cast<int64_t>(a->src[1].nb[2] / 4), out, out_hs,
+                                        xr, out, outr, static_cast<int>(a->src[1].ne[1]),
                                         a->flags, s));
     }
     // phase 2: merge the partial records, then W_UV (one node, two launches)
@@ -338,8 +428,8 @@ int m4b_phase(const m4b_phase_args* a, m4b_stream_t stream) {
                                         static_cast<int>(a->src[1].ne[2]), attn, attn_hs,
                                         a->flags & M4B_FLAG_PDL, s);
     if (e != cudaSuccess) return M4B_ECUDA;
-    return status_of(launch_wvb_f16(a->src[0].data, attn, attn_hs, out, out_hs,
-                                    a->flags & M4B_FLAG_PDL, s));
+    return status_of(launch_wvb_f16(a->src[0].data, attn, Rows{attn_hs, 0}, out, Rows{out_hs, 0},
+                                    1, a->flags & M4B_FLAG_PDL, s));
 }
 
 int m4b_supports_op(int op, const m4b_tensor* srcs, int n_srcs, const m4b_tensor* dst,
@@ -395,7 +485,7 @@ int m4b_device_status(m4b_stream_t stream) {
     if (v != 0) {
         const unsigned int zero = 0;
         if (cudaMemcpyToSymbol(g_status, &zero, sizeof(zero)) != cudaSuccess) return M4B_ECUDA;
-        return M4B_ETIMEOUT;
+        return v == DEV_STATUS_BADSEQ ? M4B_EINVAL : M4B_ETIMEOUT;
     }
     return M4B_OK;
 }

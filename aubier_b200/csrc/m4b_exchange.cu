@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(THREADS)
 publish_kernel(const float* __restrict__ part, int S, PeerPtrs peers, char* local, int world,
                int rank, Layout L) {
     extern __shared__ float s_alpha[];   // [S]
-    __shared__ float s_red[THREADS / 32][128];
+    __shared__ __align__(16) float s_red[THREADS / 32][128];   // written as float4
     __shared__ float s_m[THREADS / 32], s_l[THREADS / 32];
     pdl_wait();
     const int h = blockIdx.x;

@@ -27,6 +27,7 @@ constexpr int kPartL = kLatent + 1;
 constexpr int kTileKeys = 128;   // keys per KQKV tile (the tcgen05 MMA M dimension)
 constexpr int kMaxSplits = 148;  // one persistent CTA per B200 SM
 constexpr int kMaxWorld = 8;     // GPUs of one node in the KV-slab exchange
+constexpr int kMaxSeqs = 64;     // tokens (windows) of one ragged KQKV call
 
 struct KqkvLaunch {
     const void* kcache;
@@ -34,11 +35,15 @@ struct KqkvLaunch {
     int64_t n_kv;
     const float* q;
     int64_t q_head_stride;  // floats
-    const float* mask;      // nullable
+    int64_t q_token_stride; // floats (ragged batch)
+    const float* mask;      // nullable; single-window op only
     float kq_scale;
-    int splits;
-    float* part;            // [splits][kHeads][kPartStride]
+    int splits;             // CTAs
+    float* part;            // records: [splits][kHeads][kPartStride], ragged [splits + n_seq - 1]
     uint32_t flags;
+    const int32_t* seq_base = nullptr;   // ragged batch: token t attends to cache rows
+    const int32_t* seq_len = nullptr;    // [seq_base[t], seq_base[t] + seq_len[t])
+    int n_seq = 0;
 };
 
 cudaError_t launch_kqkv_partials(const KqkvLaunch& a, cudaStream_t stream);
@@ -47,17 +52,32 @@ cudaError_t launch_kqkv_partials(const KqkvLaunch& a, cudaStream_t stream);
 cudaError_t launch_kqkv_combine(const float* part, int S, float* out, int64_t out_head_stride,
                                 uint32_t flags, cudaStream_t stream);
 
+// Ragged batch: merge each token's records (written by launch_kqkv_partials with seq_base set)
+// into out[t * out_ts + h * out_hs + d].
+cudaError_t launch_kqkv_ragged_combine(const float* part, const int32_t* seq_base,
+                                       const int32_t* seq_len, int n_seq, int64_t n_rows,
+                                       int splits, float* out, int64_t out_hs, int64_t out_ts,
+                                       uint32_t flags, cudaStream_t stream);
+
 // Merge S partial records into one unnormalised record per head ([32][kPartStride]).
 cudaError_t launch_kqkv_merge_records(const float* part, int S, float* out_records, uint32_t flags,
                                       cudaStream_t stream);
 
-// q_abs[h][r] = W_UK[h][r][:] . f16(q[h][:128]); W_UK contiguous f16 [32][512][128].
-cudaError_t launch_wkb_f16(const void* w, const float* q, int64_t q_head_stride, float* out,
-                           int64_t out_head_stride, uint32_t flags, cudaStream_t stream);
+// Per-token activation / output addressing of the gemvs: element (t, h, i) at t*ts + h*hs + i.
+struct Rows {
+    int64_t hs;   // head stride, floats
+    int64_t ts;   // token stride, floats
+};
 
-// out[h][j] = W_UV[h][j][:] . f16(x[h][:512]); W_UV contiguous f16 [32][128][512].
-cudaError_t launch_wvb_f16(const void* w, const float* x, int64_t x_head_stride, float* out,
-                           int64_t out_head_stride, uint32_t flags, cudaStream_t stream);
+// q_abs[t][h][r] = W_UK[h][r][:] . f16(q[t][h][:128]) for nt tokens; W_UK contiguous f16
+// [32][512][128], read once for all tokens.
+cudaError_t launch_wkb_f16(const void* w, const float* q, Rows qr, float* out, Rows outr, int nt,
+                           uint32_t flags, cudaStream_t stream);
+
+// out[t][h][j] = W_UV[h][j][:] . f16(x[t][h][:512]) for nt tokens; W_UV contiguous f16
+// [32][128][512], read once for all tokens.
+cudaError_t launch_wvb_f16(const void* w, const float* x, Rows xr, float* out, Rows outr, int nt,
+                           uint32_t flags, cudaStream_t stream);
 
 // Launch helper: plain launch, or with programmatic stream serialisation when PDL is requested.
 template <typename... KArgs, typename... Args>

@@ -21,7 +21,12 @@
 // while the softmax of tile i works (S and P are double-buffered).
 //
 // CTA = one split (a contiguous run of tiles, balanced as in m4-kqkv.cu:204-218), persistent,
-// one per SM.  Warp roles (320 threads):
+// one per SM.  Ragged batches (several tokens, each attending to its own window [base, base+len)
+// of one packed cache -- the engine's per-row mask, m1_layer.cpp:756-773) use the same kernel:
+// the tiles of all windows are concatenated and cut into balanced CTA ranges, so a CTA works
+// through a short list of segments (one per window it touches), restaging Q and writing one
+// partial record at every segment boundary.  The single-token op is the one-segment case.
+// Warp roles (320 threads):
 //   warp 0      TMA producer (ring loads)
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer; descriptors are precomputed,
 //               each MMA costs one 32-bit add to issue
@@ -59,7 +64,9 @@ constexpr int OFF_Q = OFF_RING + NSLOT * SLOT_BYTES;
 constexpr int OFF_P = OFF_Q + NCOL * QCH_BYTES;
 constexpr int OFF_CTRL = OFF_P + 2 * P_BYTES;
 constexpr int CTRL_BYTES = 2048;
-constexpr int SMEM_BYTES = OFF_CTRL + CTRL_BYTES + 1024;  // + slack to align the base to 1 KB
+constexpr int OFF_SEG = OFF_CTRL + CTRL_BYTES;
+constexpr int SEG_BYTES = kMaxSeqs * 32;
+constexpr int SMEM_BYTES = OFF_SEG + SEG_BYTES + 1024;  // + slack to align the base to 1 KB
 
 constexpr int NTHREADS = 320;
 constexpr int TMEM_COLS = 256;   // S^T x2: cols [0,64); O^T: 4 blocks of 32 cols at [64,192)
@@ -67,6 +74,18 @@ constexpr int TM_S = 0;
 constexpr int TM_O = 64;
 constexpr float RESCALE_THRESH = 8.0f;  // log2 units: P stays <= 2^8 between rescales
 constexpr float LOG2E = 1.4426950408889634f;
+
+// One run of consecutive tiles of one window, as this CTA processes it.
+struct Seg {
+    int row0;     // cache row of the segment's first key
+    int ntiles;   // tiles in the segment
+    int nvalid;   // keys at or after row0 that belong to the window (later keys are masked)
+    int seq;      // token index: selects q and, with slot, the output
+    int slot;     // partial record index
+    int first;    // CTA-local index of the segment's first tile
+    int pad[2];
+};
+static_assert(sizeof(Seg) == 32, "segment table entry");
 
 struct Ctrl {
     uint64_t full[NSLOT];
@@ -77,6 +96,8 @@ struct Ctrl {
     uint64_t redl_full[2];  // per head group: the 4 warps' row sums are in red_l[]
     uint32_t tmem_base;
     int abort_flag;
+    int nseg;     // segments of this CTA
+    int ntot;     // tiles of this CTA (sum over its segments)
     alignas(16) float red[2][2][4][16];  // [tile parity][group][quadrant][head], read as float4
     alignas(16) float red_l[2][4][16];   // [group][quadrant][head]
 };
@@ -123,23 +144,92 @@ __device__ __forceinline__ float transpose_reduce16(const float (&in)[16], int l
     return kMax ? fmaxf(v[0], r) : v[0] + r;
 }
 
+// Tiles per window for up to 64 windows, two per lane: ts = ceil(len / 128), ps = exclusive prefix
+// over the windows in token order, total = all tiles.  A window outside [0, n_rows) counts as
+// empty and raises the device status (the host never reads base / len: they may be produced on
+// the device, like the reference's kidx / pos, m4-phase.cu:265-267).
+struct SeqTiles {
+    int ts[2], ps[2], base[2], len[2];
+    int total;
+};
+
+__device__ __forceinline__ int warp_incl_scan(int v, int lane) {
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, off);
+        if (lane >= off) v += u;
+    }
+    return v;
+}
+
+__device__ SeqTiles seq_tiles(const int32_t* __restrict__ seq_base,
+                              const int32_t* __restrict__ seq_len, int n_seq, int n_rows,
+                              int lane) {
+    SeqTiles st;
+    bool bad = false;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int sq = lane + 32 * k;
+        int b = 0, l = 0;
+        if (sq < n_seq) {
+            b = __ldg(seq_base + sq);
+            l = __ldg(seq_len + sq);
+            if (b < 0 || l < 0 || static_cast<int64_t>(b) + l > n_rows) {
+                bad = true;
+                b = 0;
+                l = 0;
+            }
+        }
+        st.base[k] = b;
+        st.len[k] = l;
+        st.ts[k] = (l + TK - 1) / TK;
+    }
+    const int i0 = warp_incl_scan(st.ts[0], lane);
+    const int tot0 = __shfl_sync(0xffffffffu, i0, 31);
+    const int i1 = warp_incl_scan(st.ts[1], lane);
+    st.total = tot0 + __shfl_sync(0xffffffffu, i1, 31);
+    st.ps[0] = i0 - st.ts[0];
+    st.ps[1] = tot0 + i1 - st.ts[1];
+    if (bad) atomicExch(&g_status, DEV_STATUS_BADSEQ);
+    return st;
+}
+
+// Balanced cut of T tiles over G CTAs (m4-kqkv.cu:214-218): CTA c owns [lo(c), lo(c) + cnt(c)).
+__device__ __forceinline__ int cut_lo(int T, int G, int c) {
+    const int b = T / G, r = T % G;
+    return c * b + min(c, r);
+}
+__device__ __forceinline__ int cut_owner(int T, int G, int t) {   // the CTA owning tile t
+    const int b = T / G, r = T % G;
+    const int big = r * (b + 1);
+    return t < big ? t / (b + 1) : r + (t - big) / b;
+}
+
+struct KqParams {
+    const float* q;
+    int64_t q_hs;             // head stride, floats
+    int64_t q_ts;             // token stride, floats (ragged)
+    const float* mask;        // single-window op only, nullable
+    float kq_scale;
+    int n_rows;               // cache rows (the single-window op's n_kv)
+    float* part;
+    uint32_t flags;
+    const int32_t* seq_base;  // ragged: per-token window; nullptr for the single-window op
+    const int32_t* seq_len;
+    int n_seq;
+};
+
 __global__ void __launch_bounds__(NTHREADS, 1)
-kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __restrict__ q,
-                    int64_t q_hs, const float* __restrict__ mask, float kq_scale, int n_kv,
-                    int splits, float* __restrict__ part, uint32_t flags) {
+kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
     Ctrl& C = *reinterpret_cast<Ctrl*>(smem + OFF_CTRL);
+    Seg* const segs = reinterpret_cast<Seg*>(smem + OFF_SEG);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int split = blockIdx.x;
-
-    const int n_tiles = (n_kv + TK - 1) / TK;
-    const int base_t = n_tiles / splits;
-    const int rem = n_tiles % splits;
-    const int t0 = split * base_t + min(split, rem);
-    const int nt = base_t + (split < rem ? 1 : 0);
+    const int cta = blockIdx.x;
+    const int G = gridDim.x;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NSLOT; ++i) {
@@ -158,7 +248,56 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
         C.abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 0 && lane == 0) tma_prefetch_desc(&tmap);
+    if (warp == 0) {
+        if (lane == 0) tma_prefetch_desc(&tmap);
+        // ---- this CTA's segments
+        if (p.seq_base == nullptr) {   // one window: the whole cache, masked by p.mask
+            if (lane == 0) {
+                const int T = (p.n_rows + TK - 1) / TK;
+                const int lo = cut_lo(T, G, cta);
+                Seg sg = {};
+                sg.row0 = lo * TK;
+                sg.ntiles = cut_lo(T, G, cta + 1) - lo;
+                sg.nvalid = p.n_rows - lo * TK;
+                sg.seq = 0;
+                sg.slot = cta;
+                sg.first = 0;
+                segs[0] = sg;
+                C.nseg = 1;   // written even when empty: every split owns a record
+                C.ntot = sg.ntiles;
+            }
+        } else {
+            if (!(p.flags & M4B_FLAG_KV_STATIC)) pdl_wait();   // windows may come from the device
+            const SeqTiles st = seq_tiles(p.seq_base, p.seq_len, p.n_seq, p.n_rows, lane);
+            const int lo = cut_lo(st.total, G, cta), hi = cut_lo(st.total, G, cta + 1);
+            bool hit[2];
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+                hit[k] = st.ts[k] > 0 && st.ps[k] < hi && st.ps[k] + st.ts[k] > lo;
+            const unsigned b0 = __ballot_sync(0xffffffffu, hit[0]);
+            const unsigned b1 = __ballot_sync(0xffffffffu, hit[1]);
+            const unsigned below = (1u << lane) - 1u;
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                if (!hit[k]) continue;
+                const int idx = k == 0 ? __popc(b0 & below) : __popc(b0) + __popc(b1 & below);
+                const int a = max(lo, st.ps[k]), e = min(hi, st.ps[k] + st.ts[k]);
+                const int j0 = a - st.ps[k];
+                Seg sg = {};
+                sg.row0 = st.base[k] + j0 * TK;
+                sg.ntiles = e - a;
+                sg.nvalid = st.len[k] - j0 * TK;
+                sg.seq = lane + 32 * k;
+                sg.slot = cta + sg.seq;
+                sg.first = a - lo;
+                segs[idx] = sg;
+            }
+            if (lane == 0) {
+                C.nseg = __popc(b0) + __popc(b1);
+                C.ntot = hi - lo;
+            }
+        }
+    }
     if (warp == 1) {
         tmem_alloc(&C.tmem_base, TMEM_COLS);
         tmem_relinquish();
@@ -168,22 +307,28 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
     tc_fence_after();
     const uint32_t tmem = C.tmem_base;
     volatile int* abort_flag = &C.abort_flag;
+    const int nseg = C.nseg;
+    const int NT = C.ntot;
+    // segment holding CTA-local tile t, advancing a cursor (tiles are visited in order)
+    auto seg_of = [&](int t, int& g) -> const Seg& {
+        while (t >= segs[g].first + segs[g].ntiles) ++g;
+        return segs[g];
+    };
 
     if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer
-        if (lane == 0) {
-            if (!(flags & M4B_FLAG_KV_STATIC)) pdl_wait();
+        if (lane == 0 && NT > 0) {
+            if (!(p.flags & M4B_FLAG_KV_STATIC)) pdl_wait();
             const uint64_t pol_keep = l2_policy_evict_last();    // K pass: V is re-read soon
             const uint64_t pol_done = l2_policy_evict_first();   // V pass: last use
             int slot = 0, phase = 0, issued = 0;
             bool ok = true;
-            // one ring entry: chunks c0 (and c0 + 1 when two) of tile t
-            auto entry = [&](int t, int c0, int two, uint64_t pol) {
+            // one ring entry: chunks c0 (and c0 + 1 when two) of the tile at cache row key0
+            auto entry = [&](int key0, int c0, int two, uint64_t pol) {
                 ok = ok && mbar_wait(&C.empty[slot], phase ^ 1, abort_flag);
                 if (!ok) return;
                 mbar_arrive_expect_tx(&C.full[slot], two ? SLOT_BYTES : CHUNK_BYTES);
                 uint8_t* dst = smem + OFF_RING + slot * SLOT_BYTES;
-                const int key0 = (t0 + t) * TK;
                 tma_load_2d(dst, &tmap, 64 * c0, key0, &C.full[slot], pol);
                 if (two) tma_load_2d(dst + CHUNK_BYTES, &tmap, 64 * (c0 + 1), key0, &C.full[slot], pol);
                 ++issued;
@@ -192,13 +337,19 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
                     phase ^= 1;
                 }
             };
+            int gk = 0, gv = 0;
             // ring order = consumption order: K(0), then per tile i: K(i+1), V(i)
-            for (int t = -1; t < nt && ok; ++t) {
-                if (t + 1 < nt) {
-                    for (int e = 0; e < K_ENTRIES; ++e) entry(t + 1, 2 * e, e < 4, pol_keep);
+            for (int t = -1; t < NT && ok; ++t) {
+                if (t + 1 < NT) {
+                    const Seg& sg = seg_of(t + 1, gk);
+                    const int key0 = sg.row0 + (t + 1 - sg.first) * TK;
+                    for (int e = 0; e < K_ENTRIES; ++e) entry(key0, 2 * e, e < 4, pol_keep);
                 }
-                if (t >= 0)
-                    for (int e = 0; e < V_ENTRIES; ++e) entry(t, 2 * e, 1, pol_done);
+                if (t >= 0) {
+                    const Seg& sg = seg_of(t, gv);
+                    const int key0 = sg.row0 + (t - sg.first) * TK;
+                    for (int e = 0; e < V_ENTRIES; ++e) entry(key0, 2 * e, 1, pol_done);
+                }
             }
             if (*abort_flag) {
                 // let this CTA's own copies land before its shared memory is released
@@ -222,7 +373,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
             constexpr uint32_t U_CHUNK = CHUNK_BYTES >> 4, U_SLOT = SLOT_BYTES >> 4;
             constexpr uint32_t U_QCH = QCH_BYTES >> 4, U_P = P_BYTES >> 4;
             int slot = 0, phase = 0;
-            bool ok = mbar_wait(&C.q_full, 0, abort_flag);
+            bool ok = true;
             auto take = [&]() -> uint32_t {   // wait for the next ring entry, return its slot
                 const uint32_t s_ = slot;
                 ok = ok && mbar_wait(&C.full[slot], phase, abort_flag);
@@ -232,8 +383,11 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
                 }
                 return s_;
             };
-            // MMA1 of tile t into S[t & 1]
+            int g1 = 0, g2 = 0;
+            // MMA1 of tile t into S[t & 1]; the first tile of segment g waits for its Q
             auto mma1 = [&](int t) {
+                const Seg& sg = seg_of(t, g1);
+                if (t == sg.first) ok = ok && mbar_wait(&C.q_full, g1 & 1, abort_flag);
                 const uint32_t dS = tmem + TM_S + 32 * (t & 1);
                 for (int e = 0; e < K_ENTRIES && ok; ++e) {
                     const uint32_t sl = take();
@@ -254,15 +408,17 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
                 }
                 if (ok) mma_commit(&C.s_full[t & 1]);
             };
-            if (nt > 0) mma1(0);
-            for (int i = 0; i < nt && ok; ++i) {
-                if (i + 1 < nt) mma1(i + 1);
-                // MMA2 of tile i: needs its P, then the 4 latent blocks of the V pass
+            if (NT > 0) mma1(0);
+            for (int i = 0; i < NT && ok; ++i) {
+                if (i + 1 < NT) mma1(i + 1);
+                // MMA2 of tile i: needs its P, then the 4 latent blocks of the V pass; the first
+                // tile of a segment starts a fresh accumulator
+                const Seg& sg = seg_of(i, g2);
                 ok = ok && mbar_wait(&C.p_full[i & 1], (i >> 1) & 1, abort_flag);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t b0 = lo_p + (i & 1) * U_P;
-                const uint32_t acc0 = i > 0 ? 1u : 0u;
+                const uint32_t acc0 = i != sg.first ? 1u : 0u;
                 for (int b = 0; b < V_ENTRIES && ok; ++b) {
                     const uint32_t sl = take();
                     if (!ok) break;
@@ -287,24 +443,27 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
         const int key_in_tile = quad * 32 + lane;   // M = 128 layout: lane = row
         const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
 
-        // Stage Q (f32 -> f16, round to nearest even) into the K-major SW128 layout.
+        // Stage one token's Q (f32 -> f16, round to nearest even) into the K-major SW128 layout.
+        auto stage_q = [&](const float* qs) {
+            for (int u = threadIdx.x - 64; u < H * (D / 8); u += 256) {
+                const int h = u / (D / 8);
+                const int col = (u % (D / 8)) * 8;
+                const float* src = qs + h * p.q_hs + col;
+                uint4 pk;
+                pk.x = pack_half2(src[0], src[1]);
+                pk.y = pack_half2(src[2], src[3]);
+                pk.z = pack_half2(src[4], src[5]);
+                pk.w = pack_half2(src[6], src[7]);
+                const int chunk = col >> 6;
+                const int unit = (col & 63) >> 3;
+                *reinterpret_cast<uint4*>(smem + OFF_Q + chunk * QCH_BYTES + h * 128 +
+                                          ((unit ^ (h & 7)) << 4)) = pk;
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&C.q_full);
+        };
         pdl_wait();
-        for (int u = threadIdx.x - 64; u < H * (D / 8); u += 256) {
-            const int h = u / (D / 8);
-            const int col = (u % (D / 8)) * 8;
-            const float* src = q + h * q_hs + col;
-            uint4 pk;
-            pk.x = pack_half2(src[0], src[1]);
-            pk.y = pack_half2(src[2], src[3]);
-            pk.z = pack_half2(src[4], src[5]);
-            pk.w = pack_half2(src[6], src[7]);
-            const int chunk = col >> 6;
-            const int unit = (col & 63) >> 3;
-            *reinterpret_cast<uint4*>(smem + OFF_Q + chunk * QCH_BYTES + h * 128 +
-                                      ((unit ^ (h & 7)) << 4)) = pk;
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(&C.q_full);
+        if (NT > 0) stage_q(p.q + segs[0].seq * p.q_ts);
 
         // P destination of this thread's key: column key_in_tile of the 32 head rows, K-major,
         // as two 64-key chunks of 4 KB
@@ -318,20 +477,69 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
             l_part[j] = 0.0f;
         }
         bool ok = true;
-        for (int i = 0; i < nt; ++i) {
-            const int kg = (t0 + i) * TK + key_in_tile;
-            const bool valid = kg < n_kv;
+        int nflush = 0;
+        // ---- a segment's partial record (o[512], m, l) per head; o is read from TMEM once the
+        // segment's last MMA2 is complete (bar, parity)
+        auto flush = [&](const Seg& sg, uint64_t* bar, uint32_t parity) {
+            float* prec = p.part + static_cast<size_t>(sg.slot) * H * kPartStride;
+            const float lsum = transpose_reduce16<false>(l_part, lane);
+            if (ok) {
+                if ((lane & 1) == 0) C.red_l[grp][quad][lane >> 1] = lsum;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&C.redl_full[grp]);
+                ok = warp_wait(&C.redl_full[grp], nflush & 1, abort_flag);
+            }
+            ++nflush;
+            if (ok && quad == 0 && lane < 16) {
+                const int h = 16 * grp + lane;
+                const float l = C.red_l[grp][0][lane] + C.red_l[grp][1][lane] +
+                                C.red_l[grp][2][lane] + C.red_l[grp][3][lane];
+                float m = -INFINITY;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (lane == j) m = m_run[j];
+                prec[h * kPartStride + kPartM] = m;
+                prec[h * kPartStride + kPartL] = l;
+            }
+            if (!ok) return;
+            ok = warp_wait(bar, parity, abort_flag);
+            if (!ok) return;
+            tc_fence_after();
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                float o[16];
+                if (sg.ntiles > 0) {
+                    tmem_ld16(tmem + lane_off + TM_O + 32 * b + 16 * grp, o);
+                    tmem_wait_ld();
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) o[j] = 0.0f;   // an empty split: o = 0
+                }
+                const int d = 128 * b + quad * 32 + lane;   // M = 128 layout: every lane is a row
+#pragma unroll
+                for (int j = 0; j < 16; ++j) prec[(16 * grp + j) * kPartStride + d] = o[j];
+            }
+        };
+
+        int g = 0;
+        for (int i = 0; i < NT; ++i) {
+            const Seg& sg = seg_of(i, g);
+            const int kl = (i - sg.first) * TK + key_in_tile;   // key index from the segment start
+            const bool valid = kl < sg.nvalid;
             float mv = 0.0f;
-            if (valid && mask != nullptr) mv = __ldg(mask + kg);
+            if (valid && p.mask != nullptr) mv = __ldg(p.mask + sg.row0 + kl);
             ok = warp_wait(&C.s_full[i & 1], (i >> 1) & 1, abort_flag);
             if (!ok) break;
             tc_fence_after();
             float s[16];
             tmem_ld16(tmem + lane_off + TM_S + 32 * (i & 1) + 16 * grp, s);
             tmem_wait_ld();
+            // MMA1(i) is complete, so Q is free: the next segment's token goes in now
+            const bool seg_end = (i == sg.first + sg.ntiles - 1);
+            if (seg_end && g + 1 < nseg) stage_q(p.q + segs[g + 1].seq * p.q_ts);
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-                float t = s[j] * kq_scale;   // soft_max_ext: scale, then add the mask
+                float t = s[j] * p.kq_scale;   // soft_max_ext: scale, then add the mask
                 t = t + mv;
                 s[j] = valid ? t * LOG2E : -INFINITY;
             }
@@ -374,7 +582,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
                 }
             }
             if (need) {   // uniform across the group: every thread computed the same maxima
-                // O holds the sum through tile i-1: wait for MMA2(i-1) before rescaling it
+                // O holds the sum through tile i-1 (same segment): wait for MMA2(i-1)
                 ok = warp_wait(&C.o_done, (i - 1) & 1, abort_flag);
                 if (!ok) break;
                 tc_fence_after();
@@ -395,50 +603,30 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
             uint8_t* const prow = prow0 + (i & 1) * P_BYTES;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-                const float p = (s[j] == -INFINITY) ? 0.0f : exp2f(s[j] - m_run[j]);
-                l_part[j] += p;
+                const float pv = (s[j] == -INFINITY) ? 0.0f : exp2f(s[j] - m_run[j]);
+                l_part[j] += pv;
                 const int h = 16 * grp + j;
                 *reinterpret_cast<__half*>(prow + h * 128 + ((punit ^ (h & 7)) << 4)) =
-                    __float2half_rn(p);
+                    __float2half_rn(pv);
             }
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&C.p_full[i & 1]);
-        }
-
-        // ---- epilogue: the split's partial record (o[512], m, l) per head
-        float* prec = part + static_cast<size_t>(split) * H * kPartStride;
-        const float lsum = transpose_reduce16<false>(l_part, lane);
-        if (ok) {
-            if ((lane & 1) == 0) C.red_l[grp][quad][lane >> 1] = lsum;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&C.redl_full[grp]);
-            ok = warp_wait(&C.redl_full[grp], 0, abort_flag);
-        }
-        if (ok && quad == 0 && lane < 16) {
-            const int h = 16 * grp + lane;
-            const float l = C.red_l[grp][0][lane] + C.red_l[grp][1][lane] +
-                            C.red_l[grp][2][lane] + C.red_l[grp][3][lane];
-            float m = -INFINITY;
+            if (seg_end && g + 1 < nseg) {
+                // a segment other than the last ends here: write its record once MMA2(i) is
+                // done (the next segment's MMA2 waits for P(i+1), written after this)
+                flush(sg, &C.o_done, i & 1);
+                if (!ok) break;
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-                if (lane == j) m = m_run[j];
-            prec[h * kPartStride + kPartM] = m;
-            prec[h * kPartStride + kPartL] = l;
-        }
-        if (warp_wait(&C.o_full, 0, abort_flag) && ok) {
-            tc_fence_after();
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                float o[16];
-                tmem_ld16(tmem + lane_off + TM_O + 32 * b + 16 * grp, o);
-                tmem_wait_ld();
-                const int d = 128 * b + quad * 32 + lane;   // M = 128 layout: every lane is a row
-#pragma unroll
-                for (int j = 0; j < 16; ++j) prec[(16 * grp + j) * kPartStride + d] = o[j];
+                for (int j = 0; j < 16; ++j) {
+                    m_run[j] = -INFINITY;
+                    l_part[j] = 0.0f;
+                }
             }
         }
+        // ---- the last segment's record (every split of the single-window op has one)
+        if (ok && nseg > 0) flush(segs[nseg - 1], &C.o_full, 0);
     }
 
     tc_fence_before();
@@ -456,21 +644,17 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const float* __res
 // memory at the end.  S may exceed one GPU's split count (records gathered from other GPUs).
 constexpr int CMB_THREADS = 256;
 
-// record_out == 0: out[h * out_hs + d] = merged, normalised attention.
-// record_out != 0: out is a record array [32][kPartStride]: the merged, unnormalised record
+// ph = head h's record of the first split; records are ss floats apart.
+// record_out == 0: out[d] = merged, normalised attention (out = the head's output row).
+// record_out != 0: out = the head's record [kPartStride]: the merged, unnormalised record
 // (o = sum a_s o_s, m = m*, l = sum a_s l_s) -- the form that is exchanged between GPUs.
-__global__ void __launch_bounds__(CMB_THREADS)
-kqkv_combine_kernel(const float* __restrict__ part, int S, float* __restrict__ out, int64_t out_hs,
-                    int record_out) {
-    extern __shared__ float s_alpha[];   // [S]
-    __shared__ float s_red[CMB_THREADS / 32][128];
+__device__ __forceinline__ void merge_head(const float* __restrict__ ph, int S, size_t ss,
+                                           float* __restrict__ out, int record_out,
+                                           float* s_alpha) {
+    __shared__ __align__(16) float s_red[CMB_THREADS / 32][128];   // written as float4
     __shared__ float s_m[CMB_THREADS / 32], s_l[CMB_THREADS / 32];
-    pdl_wait();
-    const int h = blockIdx.x;
     const int d0 = blockIdx.y * 128;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const size_t ss = static_cast<size_t>(H) * kPartStride;
-    const float* ph = part + static_cast<size_t>(h) * kPartStride;
 
     float m = -INFINITY;
     for (int s = tid; s < S; s += CMB_THREADS) m = fmaxf(m, __ldg(ph + s * ss + kPartM));
@@ -515,18 +699,68 @@ kqkv_combine_kernel(const float* __restrict__ part, int S, float* __restrict__ o
             l += s_l[w];
         }
         if (record_out) {
-            float* rec = out + static_cast<size_t>(h) * kPartStride;
-            rec[d0 + tid] = o;
+            out[d0 + tid] = o;
             if (blockIdx.y == 0 && tid == 0) {
-                rec[kPartM] = mstar;
-                rec[kPartL] = l;
-                rec[kPartL + 1] = 0.0f;
-                rec[kPartL + 2] = 0.0f;
+                out[kPartM] = mstar;
+                out[kPartL] = l;
+                out[kPartL + 1] = 0.0f;
+                out[kPartL + 2] = 0.0f;
             }
         } else {
-            out[h * out_hs + d0 + tid] = (mstar > -INFINITY) ? o / l : 0.0f;
+            out[d0 + tid] = (mstar > -INFINITY) ? o / l : 0.0f;
         }
     }
+}
+
+// grid (32 heads, 4 blocks of 128 columns).  record_out: see merge_head; out_hs = the output's
+// head stride in floats (kPartStride for records).
+__global__ void __launch_bounds__(CMB_THREADS)
+kqkv_combine_kernel(const float* __restrict__ part, int S, float* __restrict__ out, int64_t out_hs,
+                    int record_out) {
+    extern __shared__ float s_alpha[];   // [S]
+    pdl_wait();
+    const int h = blockIdx.x;
+    merge_head(part + static_cast<size_t>(h) * kPartStride, S,
+               static_cast<size_t>(H) * kPartStride, out + h * out_hs, record_out, s_alpha);
+}
+
+// Ragged batch: grid (32 heads, 4 column blocks, n_seq tokens).  Token t's window covers tiles
+// [ps, ps + ts) of the concatenation; the CTAs owning them wrote their records for t at slots
+// c + t (kqkv_partial_kernel), so the records to merge are the contiguous slots
+// [c_first + t, c_last + t].  An empty window gives 0 (m4-kqkv.cu:337).
+__global__ void __launch_bounds__(CMB_THREADS)
+kqkv_ragged_combine_kernel(const float* __restrict__ part, const int32_t* __restrict__ seq_base,
+                           const int32_t* __restrict__ seq_len, int n_seq, int n_rows, int G,
+                           float* __restrict__ out, int64_t out_hs, int64_t out_ts) {
+    __shared__ float s_alpha[kMaxSplits];
+    __shared__ int s_first, s_count;
+    pdl_wait();
+    const int h = blockIdx.x;
+    const int t = blockIdx.z;
+    if (threadIdx.x < 32) {
+        const SeqTiles st = seq_tiles(seq_base, seq_len, n_seq, n_rows, threadIdx.x);
+        const int k = t >> 5;
+        const int ts = __shfl_sync(0xffffffffu, k ? st.ts[1] : st.ts[0], t & 31);
+        const int ps = __shfl_sync(0xffffffffu, k ? st.ps[1] : st.ps[0], t & 31);
+        if (threadIdx.x == 0) {
+            if (ts == 0) {
+                s_first = 0;
+                s_count = 0;
+            } else {
+                s_first = cut_owner(st.total, G, ps);
+                s_count = cut_owner(st.total, G, ps + ts - 1) - s_first + 1;
+            }
+        }
+    }
+    __syncthreads();
+    float* orow = out + t * out_ts + h * out_hs;
+    if (s_count == 0) {
+        if (threadIdx.x < 128) orow[blockIdx.y * 128 + threadIdx.x] = 0.0f;
+        return;
+    }
+    const size_t ss = static_cast<size_t>(H) * kPartStride;
+    merge_head(part + static_cast<size_t>(s_first + t) * ss + static_cast<size_t>(h) * kPartStride,
+               s_count, ss, orow, 0, s_alpha);
 }
 
 }  // namespace kq
@@ -564,9 +798,20 @@ cudaError_t launch_kqkv_partials(const KqkvLaunch& a, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         if (dev < 64) attr_set |= 1ull << dev;
     }
+    KqParams p;
+    p.q = a.q;
+    p.q_hs = a.q_head_stride;
+    p.q_ts = a.q_token_stride;
+    p.mask = a.mask;
+    p.kq_scale = a.kq_scale;
+    p.n_rows = static_cast<int>(a.n_kv);
+    p.part = a.part;
+    p.flags = a.flags;
+    p.seq_base = a.seq_base;
+    p.seq_len = a.seq_len;
+    p.n_seq = a.n_seq;
     return launch(kqkv_partial_kernel, dim3(a.splits), dim3(NTHREADS), SMEM_BYTES, stream, a.flags,
-                  tmap, a.q, a.q_head_stride, a.mask, a.kq_scale, static_cast<int>(a.n_kv),
-                  a.splits, a.part, a.flags);
+                  tmap, p);
 }
 
 cudaError_t launch_kqkv_combine(const float* part, int S, float* out, int64_t out_hs,
@@ -575,6 +820,15 @@ cudaError_t launch_kqkv_combine(const float* part, int S, float* out, int64_t ou
     if (smem > 48 * 1024) return cudaErrorInvalidValue;   // > 12288 records: not a real config
     return launch(kq::kqkv_combine_kernel, dim3(kHeads, kLatent / 128), dim3(kq::CMB_THREADS), smem,
                   stream, flags, part, S, out, out_hs, 0);
+}
+
+cudaError_t launch_kqkv_ragged_combine(const float* part, const int32_t* seq_base,
+                                       const int32_t* seq_len, int n_seq, int64_t n_rows,
+                                       int splits, float* out, int64_t out_hs, int64_t out_ts,
+                                       uint32_t flags, cudaStream_t stream) {
+    return launch(kq::kqkv_ragged_combine_kernel, dim3(kHeads, kLatent / 128, n_seq),
+                  dim3(kq::CMB_THREADS), 0, stream, flags, part, seq_base, seq_len, n_seq,
+                  static_cast<int>(n_rows), splits, out, out_hs, out_ts);
 }
 
 cudaError_t launch_kqkv_merge_records(const float* part, int S, float* out_records, uint32_t flags,

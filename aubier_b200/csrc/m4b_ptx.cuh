@@ -19,7 +19,8 @@ namespace m4b {
 // Defined here: the library is one translation unit (m4b_lib.cu).
 __device__ unsigned int g_status = 0;
 
-enum : unsigned int { DEV_STATUS_OK = 0, DEV_STATUS_TIMEOUT = 1 };
+// DEV_STATUS_BADSEQ: a ragged window outside the cache (the window was treated as empty).
+enum : unsigned int { DEV_STATUS_OK = 0, DEV_STATUS_TIMEOUT = 1, DEV_STATUS_BADSEQ = 2 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

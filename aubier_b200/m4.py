@@ -61,6 +61,12 @@ class PhaseArgs(ctypes.Structure):
                 ("flags", c_uint32), ("scratch", c_void_p), ("scratch_bytes", c_uint64)]
 
 
+class RaggedArgs(ctypes.Structure):
+    _fields_ = [("kcache", Tensor), ("q", Tensor), ("seq_base", Tensor), ("seq_len", Tensor),
+                ("dst", Tensor), ("kq_scale", c_float), ("flags", c_uint32),
+                ("scratch", c_void_p), ("scratch_bytes", c_uint64)]
+
+
 class M4Error(RuntimeError):
     def __init__(self, code: int, what: str):
         self.code = code
@@ -77,6 +83,9 @@ def _load():
     for name in ("m4b_kqkv", "m4b_kqkv_partials"):
         getattr(lib, name).argtypes = [ctypes.POINTER(KqkvArgs), c_void_p]
     lib.m4b_phase.argtypes = [ctypes.POINTER(PhaseArgs), c_void_p]
+    lib.m4b_kqkv_ragged.argtypes = [ctypes.POINTER(RaggedArgs), c_void_p]
+    lib.m4b_kqkv_ragged_scratch_bytes.argtypes = [c_int64]
+    lib.m4b_kqkv_ragged_scratch_bytes.restype = c_uint64
     lib.m4b_kqkv_scratch_bytes.argtypes = [c_int, c_int64]
     lib.m4b_kqkv_scratch_bytes.restype = c_uint64
     lib.m4b_phase_scratch_bytes.argtypes = [c_int]
@@ -153,6 +162,19 @@ def _heads_desc(t: torch.Tensor, inner: int) -> Tensor:
     return gtensor(t, [inner, 1, t.shape[0], 1], [es, inner * es, hs, hs * t.shape[0]])
 
 
+def _tokens_desc(t: torch.Tensor, inner: int, token_dim: int) -> Tensor:
+    """ggml view of a (T, heads, >=inner) tensor with unit inner stride: [inner, heads, T] when
+    token_dim == 2 (q, q_abs), [inner, T, heads] when token_dim == 1 (g_kqv, W_UV in/out)."""
+    if t.dim() != 3 or t.shape[2] != inner or t.stride(2) != 1:
+        raise M4Error(EINVAL, f"expected a (tokens, heads, {inner}) view, got {tuple(t.shape)}")
+    es = t.element_size()
+    T, Hh = t.shape[0], t.shape[1]
+    ts, hs = t.stride(0) * es, t.stride(1) * es
+    if token_dim == 2:
+        return gtensor(t, [inner, Hh, T, 1], [es, hs, ts, ts * T])
+    return gtensor(t, [inner, T, Hh, 1], [es, ts, hs, hs * Hh])
+
+
 def _need_cuda(name: str, *ts):
     for t in ts:
         if t is not None and not t.is_cuda:
@@ -178,11 +200,16 @@ def wkb(w_uk: torch.Tensor, q_nope: torch.Tensor, out: torch.Tensor | None = Non
     of Qcur)."""
     _need_cuda("GGML_OP_M4_WKB", w_uk, q_nope, out)
     if out is None:
-        out = torch.empty(HEADS, LATENT, device=w_uk.device, dtype=torch.float32)
+        shape = (HEADS, LATENT) if q_nope.dim() == 2 else (q_nope.shape[0], HEADS, LATENT)
+        out = torch.empty(shape, device=w_uk.device, dtype=torch.float32)
     a = WkbArgs()
     a.src0 = gtensor(w_uk, list(reversed(w_uk.shape)))
-    a.src1 = _rows_desc(q_nope, q_nope.shape[1], q_nope.shape[0])
-    a.dst = _rows_desc(out, out.shape[1], out.shape[0])
+    if q_nope.dim() == 3:   # a batch of tokens (T, 32, 128) -> (T, 32, 512)
+        a.src1 = _tokens_desc(q_nope, q_nope.shape[2], 2)
+        a.dst = _tokens_desc(out, out.shape[2], 2)
+    else:
+        a.src1 = _rows_desc(q_nope, q_nope.shape[1], q_nope.shape[0])
+        a.dst = _rows_desc(out, out.shape[1], out.shape[0])
     a.flags = flags
     _check(_lib.m4b_wkb(ctypes.byref(a), _stream()), "m4b_wkb")
     return out
@@ -243,6 +270,39 @@ def kqkv_partials(kcache: torch.Tensor, q: torch.Tensor, mask: torch.Tensor | No
     return out
 
 
+def kqkv_ragged_scratch_bytes(n_tokens: int) -> int:
+    return int(_lib.m4b_kqkv_ragged_scratch_bytes(n_tokens))
+
+
+def kqkv_ragged(kcache: torch.Tensor, q: torch.Tensor, seq_base: torch.Tensor,
+                seq_len: torch.Tensor, kq_scale: float, out: torch.Tensor | None = None,
+                scratch: torch.Tensor | None = None, flags: int = 0) -> torch.Tensor:
+    """Ragged batch KQKV (additive op): token t attends to cache rows
+    [seq_base[t], seq_base[t] + seq_len[t]).  kcache f16 (R, 576); q f32 (T, 32, 576);
+    seq_base / seq_len int32 (T,) on the device; out f32 (T, 32, 512)."""
+    _need_cuda("m4b_kqkv_ragged", kcache, q, seq_base, seq_len, out, scratch)
+    T = q.shape[0]
+    if out is None:
+        out = torch.empty(T, HEADS, LATENT, device=q.device, dtype=torch.float32)
+    if scratch is None:
+        scratch = torch.empty(max(kqkv_ragged_scratch_bytes(T), 16), device=q.device,
+                              dtype=torch.uint8)
+    a = RaggedArgs()
+    a.kcache = _rows_desc(kcache, kcache.shape[1], kcache.shape[0])
+    a.q = _tokens_desc(q, q.shape[2], 2)
+    for name, t in (("seq_base", seq_base), ("seq_len", seq_len)):
+        if t.dtype != torch.int32 or t.dim() != 1 or t.stride(0) != 1:
+            raise M4Error(EINVAL, f"{name} must be a contiguous 1-D int32 tensor")
+        setattr(a, name, gtensor(t, [t.shape[0], 1, 1, 1]))
+    a.dst = _tokens_desc(out, LATENT, 1)
+    a.kq_scale = float(kq_scale)
+    a.flags = flags
+    a.scratch = scratch.data_ptr()
+    a.scratch_bytes = scratch.numel() * scratch.element_size()
+    _check(_lib.m4b_kqkv_ragged(ctypes.byref(a), _stream()), "m4b_kqkv_ragged")
+    return out
+
+
 def _phase(phase: int, srcs, dst: Tensor, flags: int, scratch=None) -> None:
     a = PhaseArgs()
     for i, s in enumerate(srcs):
@@ -263,9 +323,13 @@ def phase_wvb(w_uv: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = No
     x f32 (32, 512) (any row stride); out f32 (32, 128)."""
     _need_cuda("GGML_OP_M4_PHASE", w_uv, x, out)
     if out is None:
-        out = torch.empty(HEADS, VHEAD, device=x.device, dtype=torch.float32)
-    _phase(PHASE_WVB, [gtensor(w_uv, list(reversed(w_uv.shape))), _heads_desc(x, LATENT)],
-           _heads_desc(out, VHEAD), flags)
+        shape = (HEADS, VHEAD) if x.dim() == 2 else (x.shape[0], HEADS, VHEAD)
+        out = torch.empty(shape, device=x.device, dtype=torch.float32)
+    if x.dim() == 3:   # a batch of tokens (T, 32, 512) -> (T, 32, 128)
+        xd, od = _tokens_desc(x, LATENT, 1), _tokens_desc(out, VHEAD, 1)
+    else:
+        xd, od = _heads_desc(x, LATENT), _heads_desc(out, VHEAD)
+    _phase(PHASE_WVB, [gtensor(w_uv, list(reversed(w_uv.shape))), xd], od, flags)
     return out
 
 

@@ -94,8 +94,10 @@ enum m4b_flags {
  * Replaces ggml_cuda_m4_wkb (patches/ggml-m4/m4-wkb.cu:71-86); builder ggml_m4_wkb
  * (vendor/llama.cpp/ggml/src/ggml.c:3398-3423).
  *   src0  W_UK    F16 [128, 512, 32]  (BASELINE)   |  Q8_0 [64, 256, 32]  (MISTRAL_SMALL)
- *   src1  q_nope  F32 [128, 32, 1]    any head stride nb[1] (the engine's view has 768 / 512 B)
- *   dst   q_abs   F32 [512, 32, 1]    any head stride nb[1] >= 4*ne[0] (may point into Qcur)
+ *   src1  q_nope  F32 [128, 32, T]    any head stride nb[1] (the engine's view has 768 / 512 B)
+ *   dst   q_abs   F32 [512, 32, T]    any head stride nb[1] >= 4*ne[0] (may point into Qcur)
+ * T = 1 in the reference's op.  Additively, 1 <= T <= 64 tokens (token stride nb[2]) share one
+ * read of W_UK: the ragged batch path (m4b_kqkv_ragged).
  */
 typedef struct m4b_wkb_args {
     m4b_tensor src0, src1, dst;
@@ -136,6 +138,32 @@ M4B_API int m4b_kqkv(const m4b_kqkv_args * args, m4b_stream_t stream);
 M4B_API int m4b_kqkv_partials(const m4b_kqkv_args * args, m4b_stream_t stream);
 
 /*
+ * KQKV over a ragged batch (no reference counterpart: the reference runs its fused ops only at one
+ * token per step, m1_layer.cpp:283-297, and falls back to stock ops for batches).  Token t
+ * attends to its own window of one packed cache -- rows [seq_base[t], seq_base[t] + seq_len[t]),
+ * the engine's per-row mask (m1_layer.cpp:756-773) -- with the single-token op's numerics.
+ *   kcache    F16 [576, R, 1, 1]  as src0 of m4b_kqkv (all tokens' windows, in any order)
+ *   q         F32 [576, 32, T]    per-token query: head stride nb[1], token stride nb[2]
+ *   seq_base  I32 [T]             device memory, never read on the host (it may be produced on
+ *   seq_len   I32 [T]             the device); a window outside [0, R) counts as empty and makes
+ *                                 m4b_device_status() report M4B_EINVAL
+ *   dst       F32 [512, T, 32]    token stride nb[1], head stride nb[2]; an empty window gives 0
+ * 1 <= T <= 64.  The tiles of all windows are spread evenly over the SMs, whatever the lengths.
+ * Needs scratch >= m4b_kqkv_ragged_scratch_bytes(T).  With M4B_FLAG_KV_STATIC the windows, like
+ * the cache, must not be written by the kernels immediately before this one.
+ */
+typedef struct m4b_kqkv_ragged_args {
+    m4b_tensor kcache, q, seq_base, seq_len, dst;
+    float      kq_scale;
+    uint32_t   flags;
+    void *     scratch;
+    uint64_t   scratch_bytes;
+} m4b_kqkv_ragged_args;
+
+M4B_API int m4b_kqkv_ragged(const m4b_kqkv_ragged_args * args, m4b_stream_t stream);
+M4B_API uint64_t m4b_kqkv_ragged_scratch_bytes(int64_t n_tokens);
+
+/*
  * KQKV for callers that cannot allocate (no counterpart in the reference, whose KQKV always uses
  * its own static array; here the regular entry point takes caller scratch instead).  Same
  * operands, contract and output as m4b_kqkv; args->scratch is ignored.  The split-K partial
@@ -152,8 +180,9 @@ M4B_API int m4b_kqkv_static_scratch(const m4b_kqkv_args * args, m4b_stream_t str
  * Replaces ggml_cuda_m4_phase (patches/ggml-m4/m4-phase.cu:205-277); builders
  * ggml_m4_phase_kvwrite / ggml_m4_phase_wvb (ggml.c:3461-3539).
  *   phase 0  KV-write   (MISTRAL_SMALL geometry)                          -> M4B_ENOTSUP here
- *   phase 1  WVB        src0 W_UV F16 [512, 128, 32]; src1 x F32 [512, 1, 32] (nb[2] head
- *                       stride); dst F32 [128, 1, 32]
+ *   phase 1  WVB        src0 W_UV F16 [512, 128, 32]; src1 x F32 [512, T, 32] (nb[2] head
+ *                       stride); dst F32 [128, T, 32].  T = 1 in the reference's op; additively
+ *                       1 <= T <= 64 tokens (token stride nb[1]) share one read of W_UV
  *   phase 2  COMBINE_WVB (additive selector): src0 W_UV F16 [512, 128, 32]; src1 partials
  *                       F32 [516, 32, S] (m4b_kqkv_partials layout, any S >= 1, e.g. gathered
  *                       from several GPUs); dst F32 [128, 1, 32]; optional src2 F32
@@ -234,7 +263,8 @@ M4B_API int m4b_supports_op(int op, const m4b_tensor * srcs, int n_srcs, const m
  */
 M4B_API int m4b_resolve_flag(int flag, int gpu_core, int nt, int ragged_ok, int * enabled);
 
-/* Reads and clears the device status word (M4B_OK or M4B_ETIMEOUT); synchronises the stream. */
+/* Reads and clears the device status word; synchronises the stream.  M4B_OK, M4B_ETIMEOUT (a
+   bounded wait gave up) or M4B_EINVAL (a ragged window outside the cache). */
 M4B_API int m4b_device_status(m4b_stream_t stream);
 
 M4B_API const char * m4b_strerror(int code);

@@ -90,3 +90,16 @@ def window_mask(N: int, base: int, length: int) -> np.ndarray:
     if hi > lo:
         m[lo:hi] = 0.0
     return m
+
+
+def ragged_lengths(seed: int, n: int = 16, lo: int = 512, hi: int = 65536) -> np.ndarray:
+    """Per-sequence KV lengths of the ragged batched decode (config 5: 16 sequences, lengths
+    uniform on [512, 65536] by seed)."""
+    return uniform_int(seed, n, lo, hi)
+
+
+def packed_bases(lengths, gap: int = 0) -> np.ndarray:
+    """First cache row of each sequence when the sequences are packed back to back (with
+    ``gap`` unused rows after each)."""
+    lengths = np.asarray(lengths, np.int64)
+    return np.concatenate([[0], np.cumsum(lengths + gap)[:-1]]).astype(np.int64)
