@@ -48,5 +48,20 @@ def lpt_assign(lengths: list[int], world: int) -> list[list[int]]:
     return out
 
 
+def ragged_lengths(seed: int = 5, n: int = 16, lo: int = 512, hi: int = 65536) -> list[int]:
+    """The ragged decode batch: n sequence lengths uniform on [lo, hi]."""
+    import numpy as np
+    return [int(x) for x in np.random.default_rng(seed).integers(lo, hi + 1, n)]
+
+
+def packed_bases(lengths: list[int]) -> list[int]:
+    """First cache row of each sequence when the sequences are packed back to back."""
+    out, r = [], 0
+    for n in lengths:
+        out.append(r)
+        r += n
+    return out
+
+
 def rank_loads(lengths: list[int], assignment: list[list[int]]) -> list[int]:
     return [sum(lengths[i] for i in seqs) for seqs in assignment]

@@ -1,13 +1,18 @@
 #!/usr/bin/env python
 """bench.py -- MLA decode-attention layer-steps/s on B200 for aubier's fused M4 path.
 
-Workload: one decode token over a 262,144-key latent+rope f16 KV cache, 36
-layers, each with its own seeded W_UK / W_UV / cache; 32 heads, q_nope 128, rope 64, latent 512,
-V head 128, kq_scale 1/sqrt(192).  One step = the 36 layer-steps WKB -> KQKV -> PHASE(combine +
-W_UV), captured in one CUDA graph.  With N GPUs the 262,144 keys of every layer are split into N
-contiguous slabs (strong scaling); each rank computes split-K partials over its slab and the
-each rank's partials are merged into one record per head (66 KB), all-gathered over NCCL, and
-merged again with W_UV applied.
+Workload (the default): one decode token over a 262,144-key latent+rope f16 KV
+cache, 36 layers, each with its own seeded W_UK / W_UV / cache; 32 heads, q_nope 128, rope 64,
+latent 512, V head 128, kq_scale 1/sqrt(192).  One step = the 36 layer-steps WKB -> KQKV ->
+PHASE(combine + W_UV), captured in one CUDA graph.  With N GPUs the 262,144 keys of every layer
+are split into N contiguous slabs (strong scaling): each rank computes split-K partials over its
+slab, merges them into one record per head and stores it into every peer over NVLink (fused
+exchange; --exchange nccl uses an NCCL all-gather instead), then merges all ranks' records and
+applies W_UV.
+
+--config 5: ragged batched decode, 16 sequences with one new token each, lengths uniform on
+[512, 65536] by seed, one packed cache per layer with per-sequence base/length; whole sequences
+per rank (LPT on keys), no exchange.  A layer-step covers all 16 sequences.
 
 Printed JSON line (rank 0): value = layer-steps/s of the whole job, timed on the device (max over
 ranks) around exactly --steps graph replays; e2e = the same metric with the step's queries copied
@@ -15,7 +20,7 @@ host->device and its outputs device->host inside the timed region; roofline = th
 algorithmic bytes per launch over its CUDA-event-timed average launch, against the measured HBM
 copy peak; cpu_baseline = the reference's own unfused CPU ggml graph (oracle/_ref) on this host.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 4|5]
 """
 from __future__ import annotations
 
@@ -38,17 +43,13 @@ D, DQ = R + ROPE, NOPE + ROPE
 SCALE = 1.0 / math.sqrt(DQ)
 PART = R + 4
 METRIC = "MLA decode attn layer-steps/s (262144 keys, 36 layers)"
+METRIC5 = "MLA decode attn layer-steps/s (16 ragged sequences, 36 layers)"
 UNIT = "layer-steps/s"
 
 
 def layer_bytes(n_keys: int) -> int:
     """Algorithmic bytes of one layer-step: KV once, weights once, q and the output (no mask)."""
     return 1152 * n_keys + 2 * (H * R * NOPE * 2) + H * DQ * 4 + H * V * 4
-
-
-def kqkv_bytes(n_keys: int) -> int:
-    """Algorithmic bytes of one KQKV launch: its KV slab once plus the f32 query."""
-    return 1152 * n_keys + H * D * 4
 
 
 def measured_peak():
@@ -61,9 +62,9 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
-def profiled_traffic():
-    """Per-launch DRAM bytes of the KQKV kernel from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", "kqkv_partial_n262144.md")
+def profiled_traffic(name: str):
+    """Per-launch DRAM bytes of the KQKV kernel from a committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", name)
     try:
         with open(p) as f:
             m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read())
@@ -127,50 +128,69 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------------------
 # reference arm / CPU baseline: the reference's unfused CPU ggml graph (oracle/_ref)
 # ---------------------------------------------------------------------------------------------
-def cpu_reference(n_keys: int, reps: int, warmup: int = 1, budget_s: float = 60.0):
+def _ref_graph(n_keys: int, threads: int, seed: int):
     import numpy as np
     from oracle import oracle as O
-    threads = os.cpu_count() or 1
-    rng = np.random.default_rng(4)
+    rng = np.random.default_rng(seed)
     ref = O.RefMLA(H, NOPE, ROPE, R, V, n_keys, SCALE, n_threads=threads)
     ref.set_inputs(q=rng.standard_normal((H, DQ), dtype=np.float32),
                    w_uk=(0.02 * rng.standard_normal((H, R, NOPE), dtype=np.float32)).astype(np.float16),
                    kc=rng.standard_normal((n_keys, D), dtype=np.float32).astype(np.float16),
                    mask=np.zeros(n_keys, np.float32),
                    w_uv=(0.02 * rng.standard_normal((H, V, R), dtype=np.float32)).astype(np.float16))
+    return ref
+
+
+def cpu_reference(lengths, reps: int, warmup: int = 1, budget_s: float = 60.0):
+    """The reference's CPU graph for one layer-step of the workload: one single-token graph per
+    sequence (config 4: one sequence of 262,144 keys), all host threads."""
+    from oracle import oracle as O
+    threads = os.cpu_count() or 1
+    refs = [_ref_graph(n, threads, 4 + i) for i, n in enumerate(lengths)]
     for _ in range(warmup):
-        ref.compute()
+        for r in refs:
+            r.compute()
     t0 = time.perf_counter()
     done = 0
     while done < reps:        # bounded: at most `reps` layer-steps or about budget_s seconds
-        ref.compute()
+        for r in refs:
+            r.compute()
         done += 1
         if time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
-    reps = done
-    ref.close()
-    kind = "reference"
-    return {"value": reps / dt, "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": f"{reps} x 1 layer-step at {n_keys} keys (unfused ggml-cpu graph of "
+    for r in refs:
+        r.close()
+    what = (f"{lengths[0]} keys" if len(lengths) == 1 else
+            f"{len(lengths)} sequences, {sum(lengths)} keys in all")
+    return {"value": done / dt, "unit": UNIT, "cores": threads, "kind": "reference",
+            "sample": f"{done} x 1 layer-step ({what}; unfused ggml-cpu graph of "
                       f"engine/m1_layer.cpp:437-502, {O.ref_library_path().rsplit('/', 1)[-1]})",
-            "s_per_layer_step": dt / reps, "reps": reps}
+            "s_per_layer_step": dt / done, "reps": done}
+
+
+def workload_lengths(args):
+    if args.config == 5:
+        from aubier_b200.shard import ragged_lengths
+        return ragged_lengths()
+    return [args.keys]
 
 
 def run_reference(args, rank: int) -> None:
     if rank != 0:
         return
     try:
-        cb = cpu_reference(args.keys, reps=args.steps, warmup=args.warmup)
+        cb = cpu_reference(workload_lengths(args), reps=args.steps, warmup=args.warmup)
     except Exception as e:   # the oracle library travels prebuilt; report if it does not load
         print(json.dumps({"impl": "reference", "unavailable": f"oracle/_ref not loadable: {e}"}))
         return
-    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT,
+    metric = METRIC if args.config == 4 else METRIC5
+    line = {"impl": "reference", "metric": metric, "value": cb["value"], "unit": UNIT,
             "n_gpus": args.gpus, "steps": cb["reps"], "warmup": args.warmup,
             "ms_per_step": 1e3 / cb["value"], "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": f"BASELINE config 4: 1 token, {args.keys} keys, 1 layer per step",
-                       "keys": args.keys, "layers_per_step": 1},
+            "config": {"workload": f"BASELINE config {args.config}, 1 layer per step",
+                       "keys": sum(workload_lengths(args)), "layers_per_step": 1},
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -178,61 +198,188 @@ def run_reference(args, rank: int) -> None:
 
 
 # ---------------------------------------------------------------------------------------------
-# our arm
+# our arm: the two workloads
 # ---------------------------------------------------------------------------------------------
-def run_ours(args, rank: int, world: int) -> None:
+class Workload:
+    """Per-rank device state of one workload: ``step(e2e)`` enqueues the L layer-steps (with
+    e2e=True it also moves the fresh query's rope half into Qcur), ``kq()`` the L launches of the
+    dominant kernel alone; ``q``/``out`` are the per-step input / output buffers the e2e timing
+    copies from / to the host."""
+
+    def close(self):
+        pass
+
+
+def _layer_weights(L, dev):
     import torch
-    import torch.distributed as dist
-    from aubier_b200 import m4
-
-    dev = torch.device("cuda", torch.cuda.current_device())
-    L, N = args.layers, args.keys
-    assert N % world == 0, "keys must split evenly across ranks"
-    n_loc = N // world
-    S = m4.default_splits(n_loc)
-
-    # ---- per-layer state, generated on the device from fixed seeds (weights replicated, KV slabs
-    # differ per rank); q_pe is part of the per-layer query input and is pre-placed into Qcur
     g = torch.Generator(device=dev)
-    kc, wuk, wuv, q, qcur = [], [], [], [], []
+    wuk, wuv = [], []
     for layer in range(L):
         g.manual_seed(1000 * layer + 7)
         wuk.append((0.02 * torch.randn(H, R, NOPE, device=dev, generator=g)).half())
         wuv.append((0.02 * torch.randn(H, V, R, device=dev, generator=g)).half())
-        q.append(torch.randn(H, DQ, device=dev, generator=g))
-        g.manual_seed(1000 * layer + 11 + 100003 * rank)
+    return wuk, wuv, g
+
+
+def slab_workload(args, rank, world, dev):
+    """Config 4: one token, 262,144 keys per layer, cut into one contiguous slab per rank; the
+    per-head records cross GPUs once per layer (fused NVLink exchange, or NCCL)."""
+    import torch
+    import torch.distributed as dist
+    from aubier_b200 import m4
+    L, N = args.layers, args.keys
+    assert N % world == 0, "keys must split evenly across ranks"
+    n_loc = N // world
+    S = m4.default_splits(n_loc)
+    wuk, wuv, g = _layer_weights(L, dev)
+    kc, qcur = [], []
+    q = torch.empty(L, H, DQ, device=dev)
+    for layer in range(L):
+        g.manual_seed(1000 * layer + 11 + 100003 * rank)   # weights replicated, slabs differ
         kc.append(torch.randn(n_loc, D, device=dev, generator=g).half())
+        g.manual_seed(1000 * layer + 13)
+        q[layer] = torch.randn(H, DQ, device=dev, generator=g)
         qc = torch.empty(H, D, device=dev)
-        qc[:, R:] = q[-1][:, NOPE:]
+        qc[:, R:] = q[layer][:, NOPE:]
         qcur.append(qc)
+    w = Workload()
     part = torch.empty(S, H, PART, device=dev)
-    merged = torch.empty(1, H, PART, device=dev)                 # this rank's record per head
+    merged = torch.empty(1, H, PART, device=dev)
     gathered = torch.empty(world, H, PART, device=dev) if world > 1 else part
+    attn = torch.empty(H, R, device=dev)
+    w.q, w.out = q, torch.empty(L, H, V, device=dev)
     xchg = None
     if world > 1 and args.exchange == "p2p":
         from aubier_b200.exchange import PeerExchange
         xchg = PeerExchange(world, rank)
         torch.cuda.synchronize()            # every rank's inputs exist before the first exchange
         dist.barrier()
-    attn = torch.empty(H, R, device=dev)
-    out = torch.empty(L, H, V, device=dev)
     flags = m4.FLAG_PDL
 
-    def step(with_rope_copy: bool = False):
+    def step(e2e: bool = False):
         for layer in range(L):
-            if with_rope_copy:   # e2e: the fresh query's rope half goes into Qcur as well
+            if e2e:   # the fresh query's rope half goes into Qcur as well
                 qcur[layer][:, R:].copy_(q[layer][:, NOPE:])
             m4.wkb(wuk[layer], q[layer][:, :NOPE], out=qcur[layer][:, :R], flags=flags)
             m4.kqkv_partials(kc[layer], qcur[layer], None, SCALE, out=part,
                              flags=flags | m4.FLAG_KV_STATIC)
             if xchg is not None:   # fused: merge + NVLink stores into every peer, then wait+merge
                 xchg.publish(part, flags=flags)
-                xchg.combine_wvb(wuv[layer], out=out[layer], attn_out=attn, flags=flags)
+                xchg.combine_wvb(wuv[layer], out=w.out[layer], attn_out=attn, flags=flags)
                 continue
             if world > 1:   # library collective: merge the local splits, all-gather 66 KB per rank
                 m4.phase_merge_records(part, out=merged, flags=flags)
                 dist.all_gather_into_tensor(gathered, merged)
-            m4.phase_combine_wvb(wuv[layer], gathered, out=out[layer], attn_out=attn, flags=flags)
+            m4.phase_combine_wvb(wuv[layer], gathered, out=w.out[layer], attn_out=attn, flags=flags)
+
+    def kq():
+        for layer in range(L):
+            m4.kqkv_partials(kc[layer], qcur[layer], None, SCALE, out=part,
+                             flags=m4.FLAG_PDL | m4.FLAG_KV_STATIC)
+
+    w.step, w.kq = step, kq
+    w.kq_kernel = "kqkv_partial_kernel"
+    w.kq_bytes = 1152 * n_loc + H * D * 4
+    w.job_layer_bytes = layer_bytes(N)
+    w.launches_per_step = (4 if (world == 1 or xchg is not None) else 5) * L
+    w.traffic = profiled_traffic("kqkv_partial_n262144.md")
+    if w.traffic is not None and world > 1:
+        w.traffic = w.traffic / world        # the committed capture is of the 1-GPU slab
+    w.metric = METRIC
+    w.config = {"workload": "BASELINE config 4: 1 decode token, 262144-key f16 latent+rope KV "
+                            "cache, 36 layers, 32 heads, nope 128 / rope 64 / latent 512 / V 128",
+                "keys": N, "layers": L, "keys_per_gpu": n_loc, "splits_per_gpu": S,
+                "parallelism": f"kv-slab x{world}" + (
+                    "" if world == 1 else
+                    " + fused NVLink record exchange" if xchg is not None else
+                    " + nccl all-gather of merged records"),
+                "l2": "inputs larger than L2 (36 layers x 302 MB KV per step)",
+                "step": "WKB -> KQKV split-K partials -> PHASE combine+W_UV per layer, "
+                        "one CUDA graph per step"}
+    w.close = (lambda: xchg.close()) if xchg is not None else (lambda: None)
+    w.lengths = [N]
+    return w
+
+
+def ragged_workload(args, rank, world, dev):
+    """Config 5: 16 sequences, one new token each, lengths uniform on [512, 65536] by seed, each
+    layer's cache packed with per-sequence base/length; whole sequences per rank (LPT on keys),
+    no exchange."""
+    import torch
+    from aubier_b200 import m4
+    from aubier_b200.shard import lpt_assign, packed_bases, ragged_lengths
+    L = args.layers
+    lengths = ragged_lengths()
+    mine = lpt_assign(lengths, world)[rank]
+    assert mine, "more ranks than sequences"
+    my_len = [lengths[i] for i in mine]
+    T, rows = len(mine), sum(my_len)
+    base = torch.tensor(packed_bases(my_len), dtype=torch.int32, device=dev)
+    length = torch.tensor(my_len, dtype=torch.int32, device=dev)
+    wuk, wuv, g = _layer_weights(L, dev)
+    kc, qcur = [], []
+    q = torch.empty(L, T, H, DQ, device=dev)
+    for layer in range(L):
+        parts = []
+        for i in mine:      # sequence i's cache and query depend on (layer, i), not on the rank
+            g.manual_seed(1000 * layer + 17 + 7919 * i)
+            parts.append(torch.randn(lengths[i], D, device=dev, generator=g).half())
+            q[layer, len(parts) - 1] = torch.randn(H, DQ, device=dev, generator=g)
+        kc.append(torch.cat(parts))
+        del parts
+        qc = torch.empty(T, H, D, device=dev)
+        qc[:, :, R:] = q[layer][:, :, NOPE:]
+        qcur.append(qc)
+    w = Workload()
+    w.q, w.out = q, torch.empty(L, T, H, V, device=dev)
+    attn = torch.empty(T, H, R, device=dev)
+    scratch = torch.empty(m4.kqkv_ragged_scratch_bytes(T), dtype=torch.uint8, device=dev)
+    flags = m4.FLAG_PDL
+
+    def step(e2e: bool = False):
+        for layer in range(L):
+            if e2e:
+                qcur[layer][:, :, R:].copy_(q[layer][:, :, NOPE:])
+            m4.wkb(wuk[layer], q[layer][:, :, :NOPE], out=qcur[layer][:, :, :R], flags=flags)
+            m4.kqkv_ragged(kc[layer], qcur[layer], base, length, SCALE, out=attn, scratch=scratch,
+                           flags=flags | m4.FLAG_KV_STATIC)
+            m4.phase_wvb(wuv[layer], attn, out=w.out[layer], flags=flags)
+
+    def kq():
+        for layer in range(L):
+            m4.kqkv_ragged(kc[layer], qcur[layer], base, length, SCALE, out=attn, scratch=scratch,
+                           flags=m4.FLAG_PDL | m4.FLAG_KV_STATIC)
+
+    w.step, w.kq = step, kq
+    w.kq_kernel = "kqkv_partial_kernel (ragged) + kqkv_ragged_combine_kernel"
+    w.kq_bytes = 1152 * rows + T * H * D * 4
+    w.job_layer_bytes = 1152 * sum(lengths) + 2 * (H * R * NOPE * 2) + len(lengths) * (
+        H * DQ * 4 + H * V * 4)
+    w.launches_per_step = 4 * L
+    w.traffic = profiled_traffic("kqkv_ragged_config5.md")
+    w.metric = METRIC5
+    w.config = {"workload": "BASELINE config 5: ragged batched decode, 16 sequences x 1 token, "
+                            "KV lengths uniform on [512, 65536] (seed 5), packed f16 latent+rope "
+                            "cache with per-sequence base/length, 36 layers, 32 heads",
+                "keys": sum(lengths), "layers": L, "sequences": len(lengths),
+                "keys_per_gpu": rows, "sequences_per_gpu": T,
+                "parallelism": f"sequences x{world} (LPT on keys), no exchange",
+                "l2": f"inputs larger than L2 ({L} layers x {1152 * sum(lengths) / 1e6:.0f} MB KV "
+                      "per step)",
+                "step": "WKB(16 tokens) -> ragged KQKV -> W_UV(16 tokens) per layer, "
+                        "one CUDA graph per step"}
+    w.lengths = lengths
+    return w
+
+
+def run_ours(args, rank: int, world: int) -> None:
+    import torch
+    import torch.distributed as dist
+    from aubier_b200 import m4
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    L = args.layers
+    w = (ragged_workload if args.config == 5 else slab_workload)(args, rank, world, dev)
 
     def barrier():
         if world > 1:
@@ -243,12 +390,12 @@ def run_ours(args, rank: int, world: int) -> None:
     stream.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(stream):
         for _ in range(max(1, args.warmup)):
-            step()
+            w.step()
     torch.cuda.current_stream().wait_stream(stream)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        step()
+        w.step()
     for _ in range(args.warmup):
         graph.replay()
     torch.cuda.synchronize()
@@ -271,8 +418,7 @@ def run_ours(args, rank: int, world: int) -> None:
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop() if sampler else None
-    ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], device=dev)
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
@@ -280,23 +426,20 @@ def run_ours(args, rank: int, world: int) -> None:
     value = L * args.steps / (ms_max * 1e-3)
 
     # ---- end to end: host queries in, host outputs back, every step
-    q_host = torch.randn(args.steps, L, H, DQ, pin_memory=True)
-    out_host = torch.empty(args.steps, L, H, V, pin_memory=True)
-    qbuf = torch.stack(q)                         # graph inputs are views of these buffers
-    for layer in range(L):
-        q[layer].data = qbuf[layer]
+    q_host = torch.randn((args.steps,) + tuple(w.q.shape), pin_memory=True)
+    out_host = torch.empty((args.steps,) + tuple(w.out.shape), pin_memory=True)
     graph_e2e = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph_e2e):
-        step(with_rope_copy=True)
+        w.step(e2e=True)
     graph_e2e.replay()
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
     e0.record()
     for k in range(args.steps):
-        qbuf.copy_(q_host[k], non_blocking=True)
+        w.q.copy_(q_host[k], non_blocking=True)
         graph_e2e.replay()
-        out_host[k].copy_(out, non_blocking=True)
+        out_host[k].copy_(w.out, non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
     barrier()
@@ -304,13 +447,13 @@ def run_ours(args, rank: int, world: int) -> None:
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = L * args.steps / (float(te.item()) * 1e-3)
+    h2d = w.q.numel() * 4 * world      # whole job: every rank copies its own queries
+    d2h = w.out.numel() * 4 * world
 
-    # ---- the dominant kernel alone: one graph of the L KQKV launches, CUDA events around it
+    # ---- the dominant kernel alone: one graph of its L launches, CUDA events around it
     graph_kq = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph_kq):
-        for layer in range(L):
-            m4.kqkv_partials(kc[layer], qcur[layer], None, SCALE, out=part,
-                             flags=m4.FLAG_PDL | m4.FLAG_KV_STATIC)
+        w.kq()
     graph_kq.replay()
     torch.cuda.synchronize()
     kreps = max(3, args.steps // 4)
@@ -321,15 +464,11 @@ def run_ours(args, rank: int, world: int) -> None:
     torch.cuda.synchronize()
     kq_us = e0.elapsed_time(e1) * 1e3 / (kreps * L)
     peak, peak_kind = measured_peak()
-    achieved = kqkv_bytes(n_loc) / (kq_us * 1e-6) / 1e9
-    traffic = profiled_traffic()
-    if traffic is not None and world > 1:
-        traffic = traffic / world        # the committed capture is of the 1-GPU slab
+    achieved = w.kq_bytes / (kq_us * 1e-6) / 1e9
 
     assert m4.device_status() == m4.OK
     del graph, graph_e2e, graph_kq           # release graphs before the process group
-    if xchg is not None:
-        xchg.close()                         # collective: detach, meet, free
+    w.close()                                # collective where the workload exchanges
 
     if rank != 0:
         return
@@ -337,36 +476,26 @@ def run_ours(args, rank: int, world: int) -> None:
     _restore_stdout()
     if world == 1 and not args.no_cpu_baseline:
         try:
-            cb = cpu_reference(N, reps=args.cpu_reps)
+            cb = cpu_reference(w.lengths, reps=args.cpu_reps)
             cpu_baseline = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
         except Exception as e:
             cpu_baseline = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
                             "sample": f"unavailable: {e}"}
-    step_gbs = L * layer_bytes(N) / (ms_per_step * 1e-3) / 1e9
+    step_gbs = L * w.job_layer_bytes / (ms_per_step * 1e-3) / 1e9
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "metric": w.metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": "BASELINE config 4: 1 decode token, 262144-key f16 latent+rope KV "
-                               "cache, 36 layers, 32 heads, nope 128 / rope 64 / latent 512 / V 128",
-                   "keys": N, "layers": L, "keys_per_gpu": n_loc, "splits_per_gpu": S,
-                   "parallelism": f"kv-slab x{world}" + (
-                       "" if world == 1 else
-                       " + fused NVLink record exchange" if args.exchange == "p2p" else
-                       " + nccl all-gather of merged records"),
-                   "l2": "inputs larger than L2 (36 layers x 302 MB KV per step)",
-                   "step": "WKB -> KQKV split-K partials -> PHASE combine+W_UV per layer, "
-                           "one CUDA graph per step"},
+        "config": w.config,
         "hbm_gbs_step": step_gbs,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": "kqkv_partial_kernel", "kernel_us": kq_us,
+                     "frac": achieved / peak, "traffic": w.traffic, "peak_kind": peak_kind,
+                     "kernel": w.kq_kernel, "kernel_us": kq_us,
                      "frac_of_nominal_8000": achieved / 8000.0},
         "cpu_baseline": cpu_baseline,
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": L * H * DQ * 4,
-                "d2h_bytes_per_step": L * H * V * 4},
-        "gpu_launches": (4 + (1 if world > 1 else 0)) * L * args.steps,   # p2p: publish+gather
-                                                                             # replace merge+combine
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": w.launches_per_step * args.steps,
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
@@ -404,7 +533,9 @@ def main():
     ap.add_argument("--cpu-reps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
-                    help="N>1: fused NVLink exchange in the merge kernels, or NCCL all-gather")
+                    help="config 4, N>1: fused NVLink exchange in the merge kernels, or NCCL")
+    ap.add_argument("--config", type=int, choices=[4, 5], default=4,
+                    help="4: 262,144-key slabs (the headline); 5: 16 ragged sequences")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
