@@ -477,6 +477,12 @@ int m4b_resolve_flag(int flag, int gpu_core, int nt, int ragged_ok, int* enabled
     return M4B_OK;
 }
 
+int m4b_last_cuda_error(const char** name) {
+    const int e = last_cuda_error().exchange(0);
+    if (name) *name = cudaGetErrorName(static_cast<cudaError_t>(e));
+    return e;
+}
+
 int m4b_device_status(m4b_stream_t stream) {
     unsigned int v = 0;
     if (cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess)

@@ -10,10 +10,12 @@
 // Reference kernels replaced: m4-wkb.cu:55-69 (Q8_0 geometry) and m4-phase.cu:52-89.
 //
 // PDL: the weight rows do not depend on the preceding kernel, so they are loaded into registers
-// BEFORE griddepcontrol.wait; only the activation read waits.  No kernel releases its dependent
-// early (griddepcontrol.launch_dependents): measured on a 36-layer chain, an early release let
-// the next KQKV grid occupy the SMs while this chain's small kernels still ran, and the step got
-// ~7% slower.
+// BEFORE griddepcontrol.wait; only the activation read waits.  WKB alone releases its dependent
+// (the KQKV launch) as soon as its weights are in flight: KQKV's CTAs then set up and, with a
+// static cache, start streaming it on the SMs WKB leaves free, while WKB finishes (measured
+// ~0.6 us per layer-step on the 36-layer chain).  Releasing early from every kernel was measured
+// ~7% slower: the next layer's KQKV grid then held the SMs while this layer's small kernels
+// still had to run.
 #include <cuda_fp16.h>
 
 #include "m4b_internal.h"
@@ -65,6 +67,7 @@ wkb_f16_kernel(const __half* __restrict__ w, const float* __restrict__ q, Rows q
         const int row = row0 + 2 * it + hw;
         wv[it] = ldg_stream(w + static_cast<size_t>(row) * kNope + 8 * l16);
     }
+    pdl_launch_dependents();
     pdl_wait();
     for (int t = 0; t < nt; ++t) {
         const float* qt = q + t * qr.ts + h * qr.hs + 8 * l16;

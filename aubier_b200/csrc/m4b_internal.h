@@ -1,6 +1,7 @@
 // m4b_internal.h -- declarations shared by the M4 kernel translation units (not part of the ABI).
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -79,6 +80,16 @@ cudaError_t launch_wkb_f16(const void* w, const float* q, Rows qr, float* out, R
 cudaError_t launch_wvb_f16(const void* w, const float* x, Rows xr, float* out, Rows outr, int nt,
                            uint32_t flags, cudaStream_t stream);
 
+// The last CUDA error a launch of this library hit (m4b_last_cuda_error reads and clears it).
+inline std::atomic<int>& last_cuda_error() {
+    static std::atomic<int> e{0};
+    return e;
+}
+inline cudaError_t note(cudaError_t e) {
+    if (e != cudaSuccess) last_cuda_error().store(static_cast<int>(e));
+    return e;
+}
+
 // Launch helper: plain launch, or with programmatic stream serialisation when PDL is requested.
 template <typename... KArgs, typename... Args>
 cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
@@ -95,7 +106,7 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
         cfg.attrs = attr;
         cfg.numAttrs = 1;
     }
-    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+    return note(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
 }
 
 }  // namespace m4b

@@ -38,6 +38,7 @@
 // reference CPU graph, whose mul_mat converts an F32 src1 to F16 (ggml-cpu.c:1330-1375) -- and
 // both products accumulate in f32.
 #include <cstddef>
+#include <type_traits>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
@@ -444,26 +445,61 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
         const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
 
         // Stage one token's Q (f32 -> f16, round to nearest even) into the K-major SW128 layout.
-        auto stage_q = [&](const float* qs) {
-            for (int u = threadIdx.x - 64; u < H * (D / 8); u += 256) {
-                const int h = u / (D / 8);
-                const int col = (u % (D / 8)) * 8;
-                const float* src = qs + h * p.q_hs + col;
-                uint4 pk;
-                pk.x = pack_half2(src[0], src[1]);
-                pk.y = pack_half2(src[2], src[3]);
-                pk.z = pack_half2(src[4], src[5]);
-                pk.w = pack_half2(src[6], src[7]);
-                const int chunk = col >> 6;
-                const int unit = (col & 63) >> 3;
-                *reinterpret_cast<uint4*>(smem + OFF_Q + chunk * QCH_BYTES + h * 128 +
-                                          ((unit ^ (h & 7)) << 4)) = pk;
+        // Each thread converts 9 units of 8 floats with all loads issued before their first use:
+        // one L2 round trip instead of nine dependent ones, which matters because the ring has HBM
+        // saturated by then (nine round trips measured ~6.6 us, stalling the first MMA).  At a
+        // window boundary inside the tile loop, where the softmax state is live, the loads go in
+        // two batches (5 + 4 units) to stay within the 168 registers that 10 warps per SM allow
+        // (3 warps share one 16K-register sub-partition).
+        auto stage_q = [&](const float* qs, bool one_batch) {
+            constexpr int UNITS = H * (D / 8);   // 2304 units of 8 columns
+            constexpr int PER = UNITS / 256;     // 9 per softmax thread
+            static_assert(UNITS % 256 == 0, "Q units must split evenly over the softmax threads");
+            const int tid = threadIdx.x - 64;
+            const bool vec = ((reinterpret_cast<uintptr_t>(qs) |
+                               static_cast<uintptr_t>(p.q_hs * 4)) & 15) == 0;   // uniform
+            auto batch = [&](auto k0_c, auto nk_c) {
+                constexpr int K0 = decltype(k0_c)::value, NK = decltype(nk_c)::value;
+                float4 v[NK][2];
+#pragma unroll
+                for (int k = 0; k < NK; ++k) {
+                    const int u = tid + 256 * (K0 + k);
+                    const float* src = qs + (u / (D / 8)) * p.q_hs + (u % (D / 8)) * 8;
+                    if (vec) {
+                        v[k][0] = reinterpret_cast<const float4*>(src)[0];
+                        v[k][1] = reinterpret_cast<const float4*>(src)[1];
+                    } else {
+                        v[k][0] = make_float4(src[0], src[1], src[2], src[3]);
+                        v[k][1] = make_float4(src[4], src[5], src[6], src[7]);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < NK; ++k) {
+                    const int u = tid + 256 * (K0 + k);
+                    const int h = u / (D / 8);
+                    const int col = (u % (D / 8)) * 8;
+                    uint4 pk;
+                    pk.x = pack_half2(v[k][0].x, v[k][0].y);
+                    pk.y = pack_half2(v[k][0].z, v[k][0].w);
+                    pk.z = pack_half2(v[k][1].x, v[k][1].y);
+                    pk.w = pack_half2(v[k][1].z, v[k][1].w);
+                    const int chunk = col >> 6;
+                    const int unit = (col & 63) >> 3;
+                    *reinterpret_cast<uint4*>(smem + OFF_Q + chunk * QCH_BYTES + h * 128 +
+                                              ((unit ^ (h & 7)) << 4)) = pk;
+                }
+            };
+            if (one_batch) {
+                batch(std::integral_constant<int, 0>{}, std::integral_constant<int, PER>{});
+            } else {
+                batch(std::integral_constant<int, 0>{}, std::integral_constant<int, 5>{});
+                batch(std::integral_constant<int, 5>{}, std::integral_constant<int, PER - 5>{});
             }
             fence_proxy_async_smem();
             mbar_arrive(&C.q_full);
         };
         pdl_wait();
-        if (NT > 0) stage_q(p.q + segs[0].seq * p.q_ts);
+        if (NT > 0) stage_q(p.q + segs[0].seq * p.q_ts, true);
 
         // P destination of this thread's key: column key_in_tile of the 32 head rows, K-major,
         // as two 64-key chunks of 4 KB
@@ -536,7 +572,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
             tmem_wait_ld();
             // MMA1(i) is complete, so Q is free: the next segment's token goes in now
             const bool seg_end = (i == sg.first + sg.ntiles - 1);
-            if (seg_end && g + 1 < nseg) stage_q(p.q + segs[g + 1].seq * p.q_ts);
+            if (seg_end && g + 1 < nseg) stage_q(p.q + segs[g + 1].seq * p.q_ts, false);
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 float t = s[j] * p.kq_scale;   // soft_max_ext: scale, then add the mask
@@ -774,7 +810,7 @@ cudaError_t launch_kqkv_partials(const KqkvLaunch& a, cudaStream_t stream) {
         cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
                                                          cudaEnableDefault, &qres);
         if (e != cudaSuccess || qres != cudaDriverEntryPointSuccess || fn == nullptr)
-            return e != cudaSuccess ? e : cudaErrorNotSupported;
+            return note(e != cudaSuccess ? e : cudaErrorNotSupported);
         encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
     CUtensorMap tmap;
@@ -786,7 +822,7 @@ cudaError_t launch_kqkv_partials(const KqkvLaunch& a, cudaStream_t stream) {
                         dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    if (r != CUDA_SUCCESS) return note(cudaErrorInvalidValue);
 
     static uint64_t attr_set = 0;   // one bit per device ordinal
     int dev = 0;
@@ -795,7 +831,7 @@ cudaError_t launch_kqkv_partials(const KqkvLaunch& a, cudaStream_t stream) {
     if (dev >= 64 || !((attr_set >> dev) & 1)) {
         e = cudaFuncSetAttribute(kqkv_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  SMEM_BYTES);
-        if (e != cudaSuccess) return e;
+        if (e != cudaSuccess) return note(e);
         if (dev < 64) attr_set |= 1ull << dev;
     }
     KqParams p;

@@ -95,6 +95,7 @@ def _load():
                                     ctypes.POINTER(c_int32)]
     lib.m4b_resolve_flag.argtypes = [c_int, c_int, c_int, c_int, ctypes.POINTER(c_int)]
     lib.m4b_device_status.argtypes = [c_void_p]
+    lib.m4b_last_cuda_error.argtypes = [ctypes.POINTER(ctypes.c_char_p)]
     lib.m4b_strerror.argtypes = [c_int]
     lib.m4b_strerror.restype = ctypes.c_char_p
     return lib
@@ -187,6 +188,11 @@ def _stream():
 
 def _check(rc: int, what: str):
     if rc != OK:
+        if rc == ECUDA:   # name the CUDA error behind it
+            name = ctypes.c_char_p()
+            code = _lib.m4b_last_cuda_error(ctypes.byref(name))
+            if code:
+                what = f"{what} [{(name.value or b'?').decode()} ({code})]"
         raise M4Error(rc, what)
 
 

@@ -267,6 +267,10 @@ M4B_API int m4b_resolve_flag(int flag, int gpu_core, int nt, int ragged_ok, int 
    bounded wait gave up) or M4B_EINVAL (a ragged window outside the cache). */
 M4B_API int m4b_device_status(m4b_stream_t stream);
 
+/* The last CUDA runtime error (a cudaError_t value; 0 = none) behind an M4B_ECUDA from a launch
+   entry point, with its name in *name when name is not NULL.  Reading clears it. */
+M4B_API int m4b_last_cuda_error(const char ** name);
+
 M4B_API const char * m4b_strerror(int code);
 M4B_API int          m4b_abi_version(void);
 
