@@ -346,7 +346,7 @@ M4B_API int m4b_exchange_publish(m4b_exchange* x, const m4b_phase_args* a, m4b_s
     if (!x || !a) return M4B_EINVAL;
     for (int r = 0; r < x->world; ++r)
         if (!x->peer[r]) return M4B_EINVAL;   // m4b_exchange_open not done
-    int rc = check_partials(a->src[1], 0);
+    int rc = check_partials(a->src[1], 0, kGeomBaseline);   // records of the BASELINE geometry
     if (rc != M4B_OK) return rc;
     rc = device_check(nullptr);
     if (rc != M4B_OK) return rc;
@@ -365,14 +365,16 @@ M4B_API int m4b_exchange_combine_wvb(m4b_exchange* x, const m4b_phase_args* a,
                                      m4b_stream_t stream) {
     if (!x || !a) return M4B_EINVAL;
     if (!x->local) return M4B_EINVAL;
-    int rc = check_wuv(a->src[0]);
+    int geom = 0;
+    int rc = check_wuv(a->src[0], &geom);
     if (rc != M4B_OK) return rc;
+    if (geom != kGeomBaseline) return M4B_ENOTSUP;   // the exchange carries 516-float records
     rc = check_phase_dst(a->dst);
     if (rc != M4B_OK) return rc;
     float* attn = nullptr;
     int64_t attn_hs = kLatent;
     if (a->src[2].data != nullptr) {
-        if (check_attn(a->src[2]) != M4B_OK) return M4B_EINVAL;
+        if (check_attn(a->src[2], kGeomBaseline) != M4B_OK) return M4B_EINVAL;
         attn = static_cast<float*>(a->src[2].data);
         attn_hs = static_cast<int64_t>(a->src[2].nb[2] / 4);
     }

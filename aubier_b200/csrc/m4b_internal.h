@@ -31,6 +31,7 @@ constexpr int kMaxWorld = 8;     // GPUs of one node in the KV-slab exchange
 constexpr int kMaxSeqs = 64;     // tokens (windows) of one ragged KQKV call
 
 struct KqkvLaunch {
+    int latent = kLatent;   // 512 (BASELINE) or 256 (Mistral-Small-4): selects the geometry
     const void* kcache;
     uint64_t kcache_row_bytes;
     int64_t n_kv;
@@ -49,20 +50,20 @@ struct KqkvLaunch {
 
 cudaError_t launch_kqkv_partials(const KqkvLaunch& a, cudaStream_t stream);
 
-// out[h][d] = merge over S partial records; out head stride in floats.
-cudaError_t launch_kqkv_combine(const float* part, int S, float* out, int64_t out_head_stride,
-                                uint32_t flags, cudaStream_t stream);
+// out[h][d] = merge over S partial records of latent width `latent`; out head stride in floats.
+cudaError_t launch_kqkv_combine(const float* part, int S, int latent, float* out,
+                                int64_t out_head_stride, uint32_t flags, cudaStream_t stream);
 
 // Ragged batch: merge each token's records (written by launch_kqkv_partials with seq_base set)
 // into out[t * out_ts + h * out_hs + d].
 cudaError_t launch_kqkv_ragged_combine(const float* part, const int32_t* seq_base,
                                        const int32_t* seq_len, int n_seq, int64_t n_rows,
-                                       int splits, float* out, int64_t out_hs, int64_t out_ts,
-                                       uint32_t flags, cudaStream_t stream);
+                                       int splits, int latent, float* out, int64_t out_hs,
+                                       int64_t out_ts, uint32_t flags, cudaStream_t stream);
 
-// Merge S partial records into one unnormalised record per head ([32][kPartStride]).
-cudaError_t launch_kqkv_merge_records(const float* part, int S, float* out_records, uint32_t flags,
-                                      cudaStream_t stream);
+// Merge S partial records into one unnormalised record per head ([32][latent + 4]).
+cudaError_t launch_kqkv_merge_records(const float* part, int S, int latent, float* out_records,
+                                      uint32_t flags, cudaStream_t stream);
 
 // Per-token activation / output addressing of the gemvs: element (t, h, i) at t*ts + h*hs + i.
 struct Rows {
@@ -89,6 +90,31 @@ inline cudaError_t note(cudaError_t e) {
     if (e != cudaSuccess) last_cuda_error().store(static_cast<int>(e));
     return e;
 }
+
+// Mistral-Small-4 geometry (engine/m1_layer.h:47-55): Q8_0 gemvs with the reference's Q8_1
+// activation numerics.  W_UK Q8_0 [64, 256, 32]; W_UV Q8_0 [256, 128, 32].
+cudaError_t launch_wkb_q8(const void* w, const float* q, Rows qr, float* out, Rows outr, int nt,
+                          uint32_t flags, cudaStream_t stream);
+cudaError_t launch_wvb_q8(const void* w, const float* x, Rows xr, float* out, Rows outr, int nt,
+                          uint32_t flags, cudaStream_t stream);
+
+// PHASE selector 0, the KV-write (Mistral geometry): W_kva Q8_0 [4096, 320] . Q8(cur), RMS norm of
+// the 256 latent values times norm_w, YaRN rope of the 64 rope values at position pos[0], then
+// Kcur (f32, kcur) and its f16 image into cache row kidx[0].
+struct KvWriteLaunch {
+    const float* cur;           // [4096]
+    const void* w;              // Q8_0 [4096, 320]
+    const float* norm_w;        // [256]
+    void* kcache;               // f16 rows of 320
+    int64_t kcache_row_stride;  // halves
+    int64_t kcache_rows;
+    const int64_t* kidx;        // device
+    const int32_t* pos;         // device
+    float* kcur;                // [320] out (dst)
+    float eps, freq_scale, ext_factor, attn_factor, theta_scale, corr0, corr1;
+    uint32_t flags;
+};
+cudaError_t launch_kvwrite(const KvWriteLaunch& a, cudaStream_t stream);
 
 // Launch helper: plain launch, or with programmatic stream serialisation when PDL is requested.
 template <typename... KArgs, typename... Args>

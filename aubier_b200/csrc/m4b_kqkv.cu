@@ -49,28 +49,51 @@ namespace m4b {
 namespace kq {
 
 constexpr int H = kHeads;
-constexpr int D = kKRow;                // 576
 constexpr int TK = kTileKeys;           // 128 keys per tile
-constexpr int NCOL = D / 64;            // 9 column chunks per key row
 constexpr int CHUNK_BYTES = TK * 128;   // 128 keys x 64 f16 columns = 16 KB, one SW128 TMA box
 constexpr int SLOT_BYTES = 2 * CHUNK_BYTES;
 constexpr int NSLOT = 5;                // FIFO ring: 5 x 32 KB
-constexpr int K_ENTRIES = 5;            // K pass: column chunks (0,1) (2,3) (4,5) (6,7) (8)
-constexpr int V_ENTRIES = 4;            // V pass: column chunks (0,1) (2,3) (4,5) (6,7)
 constexpr int QCH_BYTES = H * 128;      // 32 heads x 64 columns f16 = 4 KB
 constexpr int P_BYTES = 2 * QCH_BYTES;  // 32 heads x 128 keys f16 = 8 KB (double-buffered)
-
-constexpr int OFF_RING = 0;
-constexpr int OFF_Q = OFF_RING + NSLOT * SLOT_BYTES;
-constexpr int OFF_P = OFF_Q + NCOL * QCH_BYTES;
-constexpr int OFF_CTRL = OFF_P + 2 * P_BYTES;
 constexpr int CTRL_BYTES = 2048;
-constexpr int OFF_SEG = OFF_CTRL + CTRL_BYTES;
 constexpr int SEG_BYTES = kMaxSeqs * 32;
-constexpr int SMEM_BYTES = OFF_SEG + SEG_BYTES + 1024;  // + slack to align the base to 1 KB
+
+// The two head geometries (engine/m1_layer.h:47-55 and the BASELINE shape): latent R = 512 or
+// 256, rope 64.  Everything else follows from R: the K pass is the latent chunk pairs plus the
+// rope chunk, the V pass the latent pairs; one O^T block of 128 latent rows per pair.
+template <int R_>
+struct Geo {
+    static constexpr int R = R_;
+    static constexpr int D = R + kRope;                 // 576 or 320: the KV row
+    static constexpr int NCOL = D / 64;                 // 9 or 5 column chunks per key row
+    static constexpr int LAT_PAIRS = R / 128;           // 4 or 2
+    static constexpr int K_ENTRIES = LAT_PAIRS + 1;     // chunk pairs, then the rope chunk
+    static constexpr int V_ENTRIES = LAT_PAIRS;
+    static constexpr int PART = R + 4;                  // record: o[R], m, l, 2 pad
+    static constexpr int PM = R;
+    static constexpr int PL = R + 1;
+    static constexpr int OFF_RING = 0;
+    static constexpr int OFF_Q = OFF_RING + NSLOT * SLOT_BYTES;
+    static constexpr int OFF_P = OFF_Q + NCOL * QCH_BYTES;
+    static constexpr int OFF_CTRL = OFF_P + 2 * P_BYTES;
+    static constexpr int OFF_SEG = OFF_CTRL + CTRL_BYTES;
+    static constexpr int SMEM_BYTES = OFF_SEG + SEG_BYTES + 1024;   // + slack to align to 1 KB
+    // S^T x2: cols [0, 64); O^T: LAT_PAIRS blocks of 32 cols from 64 (power-of-two allocation)
+    static constexpr int TMEM_COLS = 64 + 32 * LAT_PAIRS <= 128 ? 128 : 256;
+    static constexpr int QPER = H * (D / 8) / 256;      // Q units of 8 columns per softmax thread
+    static constexpr int QB1 = (QPER + 1) / 2;          // first batch when staging in two
+    static_assert(H * (D / 8) % 256 == 0, "Q units must split evenly over the softmax threads");
+    static_assert(R % 128 == 0 && (kRope == 64), "latent in 128-column pairs, one rope chunk");
+    static_assert(OFF_Q % 1024 == 0 && OFF_P % 1024 == 0 && OFF_CTRL % 16 == 0,
+                  "TMA / UMMA operands need 1 KB alignment, vector accesses 16 B");
+    static_assert(SMEM_BYTES <= 232448, "exceeds the 227 KB per-CTA shared memory of sm_100");
+    static_assert(SMEM_BYTES < (1 << 18), "descriptor low halves assume shared addresses < 256 KB");
+    static_assert(PART * 4 % 16 == 0, "records stay 16-byte aligned");
+};
+using GeoBase = Geo<kLatent>;   // 512
+using GeoMistral = Geo<256>;
 
 constexpr int NTHREADS = 320;
-constexpr int TMEM_COLS = 256;   // S^T x2: cols [0,64); O^T: 4 blocks of 32 cols at [64,192)
 constexpr int TM_S = 0;
 constexpr int TM_O = 64;
 constexpr float RESCALE_THRESH = 8.0f;  // log2 units: P stays <= 2^8 between rescales
@@ -105,10 +128,6 @@ struct Ctrl {
 static_assert(sizeof(Ctrl) <= CTRL_BYTES, "control block too large");
 static_assert(offsetof(Ctrl, red) % 16 == 0 && offsetof(Ctrl, red_l) % 16 == 0,
               "reduction buffers are read with 16-byte vector loads");
-static_assert(OFF_Q % 1024 == 0 && OFF_P % 1024 == 0 && OFF_CTRL % 16 == 0,
-              "TMA / UMMA operands need 1 KB alignment, vector accesses 16 B");
-static_assert(SMEM_BYTES <= 232448, "exceeds the 227 KB per-CTA shared memory of sm_100");
-static_assert(SMEM_BYTES < (1 << 18), "descriptor low halves assume shared addresses < 256 KB");
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
@@ -220,17 +239,18 @@ struct KqParams {
     int n_seq;
 };
 
+template <class G>
 __global__ void __launch_bounds__(NTHREADS, 1)
 kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
-    Ctrl& C = *reinterpret_cast<Ctrl*>(smem + OFF_CTRL);
-    Seg* const segs = reinterpret_cast<Seg*>(smem + OFF_SEG);
+    Ctrl& C = *reinterpret_cast<Ctrl*>(smem + G::OFF_CTRL);
+    Seg* const segs = reinterpret_cast<Seg*>(smem + G::OFF_SEG);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int cta = blockIdx.x;
-    const int G = gridDim.x;
+    const int ncta = gridDim.x;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NSLOT; ++i) {
@@ -255,10 +275,10 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
         if (p.seq_base == nullptr) {   // one window: the whole cache, masked by p.mask
             if (lane == 0) {
                 const int T = (p.n_rows + TK - 1) / TK;
-                const int lo = cut_lo(T, G, cta);
+                const int lo = cut_lo(T, ncta, cta);
                 Seg sg = {};
                 sg.row0 = lo * TK;
-                sg.ntiles = cut_lo(T, G, cta + 1) - lo;
+                sg.ntiles = cut_lo(T, ncta, cta + 1) - lo;
                 sg.nvalid = p.n_rows - lo * TK;
                 sg.seq = 0;
                 sg.slot = cta;
@@ -270,7 +290,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
         } else {
             if (!(p.flags & M4B_FLAG_KV_STATIC)) pdl_wait();   // windows may come from the device
             const SeqTiles st = seq_tiles(p.seq_base, p.seq_len, p.n_seq, p.n_rows, lane);
-            const int lo = cut_lo(st.total, G, cta), hi = cut_lo(st.total, G, cta + 1);
+            const int lo = cut_lo(st.total, ncta, cta), hi = cut_lo(st.total, ncta, cta + 1);
             bool hit[2];
 #pragma unroll
             for (int k = 0; k < 2; ++k)
@@ -300,7 +320,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
         }
     }
     if (warp == 1) {
-        tmem_alloc(&C.tmem_base, TMEM_COLS);
+        tmem_alloc(&C.tmem_base, G::TMEM_COLS);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -329,7 +349,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
                 ok = ok && mbar_wait(&C.empty[slot], phase ^ 1, abort_flag);
                 if (!ok) return;
                 mbar_arrive_expect_tx(&C.full[slot], two ? SLOT_BYTES : CHUNK_BYTES);
-                uint8_t* dst = smem + OFF_RING + slot * SLOT_BYTES;
+                uint8_t* dst = smem + G::OFF_RING + slot * SLOT_BYTES;
                 tma_load_2d(dst, &tmap, 64 * c0, key0, &C.full[slot], pol);
                 if (two) tma_load_2d(dst + CHUNK_BYTES, &tmap, 64 * (c0 + 1), key0, &C.full[slot], pol);
                 ++issued;
@@ -344,12 +364,12 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
                 if (t + 1 < NT) {
                     const Seg& sg = seg_of(t + 1, gk);
                     const int key0 = sg.row0 + (t + 1 - sg.first) * TK;
-                    for (int e = 0; e < K_ENTRIES; ++e) entry(key0, 2 * e, e < 4, pol_keep);
+                    for (int e = 0; e < G::K_ENTRIES; ++e) entry(key0, 2 * e, e < G::LAT_PAIRS, pol_keep);
                 }
                 if (t >= 0) {
                     const Seg& sg = seg_of(t, gv);
                     const int key0 = sg.row0 + (t - sg.first) * TK;
-                    for (int e = 0; e < V_ENTRIES; ++e) entry(key0, 2 * e, 1, pol_done);
+                    for (int e = 0; e < G::V_ENTRIES; ++e) entry(key0, 2 * e, 1, pol_done);
                 }
             }
             if (*abort_flag) {
@@ -367,10 +387,10 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
             constexpr uint32_t idesc_o = idesc_f16_f32(128, 32, true, false);
             constexpr uint32_t hi = sdesc_sw128_hi(1024);   // SBO = 8 rows x 128 B
             // low descriptor halves; offsets below are in 16-byte units
-            const uint32_t lo_ringK = sdesc_sw128_lo(smem_u32(smem + OFF_RING), 16);
-            const uint32_t lo_ringMN = sdesc_sw128_lo(smem_u32(smem + OFF_RING), CHUNK_BYTES);
-            const uint32_t lo_q = sdesc_sw128_lo(smem_u32(smem + OFF_Q), 16);
-            const uint32_t lo_p = sdesc_sw128_lo(smem_u32(smem + OFF_P), 16);
+            const uint32_t lo_ringK = sdesc_sw128_lo(smem_u32(smem + G::OFF_RING), 16);
+            const uint32_t lo_ringMN = sdesc_sw128_lo(smem_u32(smem + G::OFF_RING), CHUNK_BYTES);
+            const uint32_t lo_q = sdesc_sw128_lo(smem_u32(smem + G::OFF_Q), 16);
+            const uint32_t lo_p = sdesc_sw128_lo(smem_u32(smem + G::OFF_P), 16);
             constexpr uint32_t U_CHUNK = CHUNK_BYTES >> 4, U_SLOT = SLOT_BYTES >> 4;
             constexpr uint32_t U_QCH = QCH_BYTES >> 4, U_P = P_BYTES >> 4;
             int slot = 0, phase = 0;
@@ -390,7 +410,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
                 const Seg& sg = seg_of(t, g1);
                 if (t == sg.first) ok = ok && mbar_wait(&C.q_full, g1 & 1, abort_flag);
                 const uint32_t dS = tmem + TM_S + 32 * (t & 1);
-                for (int e = 0; e < K_ENTRIES && ok; ++e) {
+                for (int e = 0; e < G::K_ENTRIES && ok; ++e) {
                     const uint32_t sl = take();
                     if (!ok) break;
                     tc_fence_after();
@@ -398,7 +418,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
                     const uint32_t b = lo_q + 2 * e * U_QCH;
 #pragma unroll
                     for (int hf = 0; hf < 2; ++hf) {
-                        if (hf == 1 && e == 4) break;
+                        if (hf == 1 && e == G::LAT_PAIRS) break;
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)
                             mma_f16(dS, sdesc_join(a + hf * U_CHUNK + 2 * kk, hi),
@@ -420,7 +440,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
                 tc_fence_after();
                 const uint32_t b0 = lo_p + (i & 1) * U_P;
                 const uint32_t acc0 = i != sg.first ? 1u : 0u;
-                for (int b = 0; b < V_ENTRIES && ok; ++b) {
+                for (int b = 0; b < G::V_ENTRIES && ok; ++b) {
                     const uint32_t sl = take();
                     if (!ok) break;
                     tc_fence_after();
@@ -449,12 +469,11 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
         // one L2 round trip instead of nine dependent ones, which matters because the ring has HBM
         // saturated by then (nine round trips measured ~6.6 us, stalling the first MMA).  At a
         // window boundary inside the tile loop, where the softmax state is live, the loads go in
-        // two batches (5 + 4 units) to stay within the 168 registers that 10 warps per SM allow
+        // two batches (5 + 4 units at BASELINE) to stay within the 168 registers that 10 warps per SM allow
         // (3 warps share one 16K-register sub-partition).
         auto stage_q = [&](const float* qs, bool one_batch) {
-            constexpr int UNITS = H * (D / 8);   // 2304 units of 8 columns
-            constexpr int PER = UNITS / 256;     // 9 per softmax thread
-            static_assert(UNITS % 256 == 0, "Q units must split evenly over the softmax threads");
+            constexpr int D = G::D;
+            constexpr int PER = G::QPER;         // 9 (BASELINE) or 5 units of 8 columns
             const int tid = threadIdx.x - 64;
             const bool vec = ((reinterpret_cast<uintptr_t>(qs) |
                                static_cast<uintptr_t>(p.q_hs * 4)) & 15) == 0;   // uniform
@@ -485,15 +504,16 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
                     pk.w = pack_half2(v[k][1].z, v[k][1].w);
                     const int chunk = col >> 6;
                     const int unit = (col & 63) >> 3;
-                    *reinterpret_cast<uint4*>(smem + OFF_Q + chunk * QCH_BYTES + h * 128 +
+                    *reinterpret_cast<uint4*>(smem + G::OFF_Q + chunk * QCH_BYTES + h * 128 +
                                               ((unit ^ (h & 7)) << 4)) = pk;
                 }
             };
             if (one_batch) {
                 batch(std::integral_constant<int, 0>{}, std::integral_constant<int, PER>{});
             } else {
-                batch(std::integral_constant<int, 0>{}, std::integral_constant<int, 5>{});
-                batch(std::integral_constant<int, 5>{}, std::integral_constant<int, PER - 5>{});
+                batch(std::integral_constant<int, 0>{}, std::integral_constant<int, G::QB1>{});
+                batch(std::integral_constant<int, G::QB1>{},
+                      std::integral_constant<int, PER - G::QB1>{});
             }
             fence_proxy_async_smem();
             mbar_arrive(&C.q_full);
@@ -503,7 +523,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
 
         // P destination of this thread's key: column key_in_tile of the 32 head rows, K-major,
         // as two 64-key chunks of 4 KB
-        uint8_t* const prow0 = smem + OFF_P + (key_in_tile >> 6) * QCH_BYTES + (key_in_tile & 7) * 2;
+        uint8_t* const prow0 = smem + G::OFF_P + (key_in_tile >> 6) * QCH_BYTES + (key_in_tile & 7) * 2;
         const int punit = (key_in_tile & 63) >> 3;
 
         float m_run[16], l_part[16];
@@ -517,7 +537,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
         // ---- a segment's partial record (o[512], m, l) per head; o is read from TMEM once the
         // segment's last MMA2 is complete (bar, parity)
         auto flush = [&](const Seg& sg, uint64_t* bar, uint32_t parity) {
-            float* prec = p.part + static_cast<size_t>(sg.slot) * H * kPartStride;
+            float* prec = p.part + static_cast<size_t>(sg.slot) * H * G::PART;
             const float lsum = transpose_reduce16<false>(l_part, lane);
             if (ok) {
                 if ((lane & 1) == 0) C.red_l[grp][quad][lane >> 1] = lsum;
@@ -534,15 +554,15 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
                     if (lane == j) m = m_run[j];
-                prec[h * kPartStride + kPartM] = m;
-                prec[h * kPartStride + kPartL] = l;
+                prec[h * G::PART + G::PM] = m;
+                prec[h * G::PART + G::PL] = l;
             }
             if (!ok) return;
             ok = warp_wait(bar, parity, abort_flag);
             if (!ok) return;
             tc_fence_after();
 #pragma unroll
-            for (int b = 0; b < 4; ++b) {
+            for (int b = 0; b < G::LAT_PAIRS; ++b) {
                 float o[16];
                 if (sg.ntiles > 0) {
                     tmem_ld16(tmem + lane_off + TM_O + 32 * b + 16 * grp, o);
@@ -553,7 +573,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
                 }
                 const int d = 128 * b + quad * 32 + lane;   // M = 128 layout: every lane is a row
 #pragma unroll
-                for (int j = 0; j < 16; ++j) prec[(16 * grp + j) * kPartStride + d] = o[j];
+                for (int j = 0; j < 16; ++j) prec[(16 * grp + j) * G::PART + d] = o[j];
             }
         };
 
@@ -625,7 +645,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
 #pragma unroll
                 for (int j = 0; j < 16; ++j) l_part[j] *= alpha[j];
 #pragma unroll
-                for (int b = 0; b < 4; ++b) {
+                for (int b = 0; b < G::LAT_PAIRS; ++b) {
                     float o[16];
                     const uint32_t ta = tmem + lane_off + TM_O + 32 * b + 16 * grp;
                     tmem_ld16(ta, o);
@@ -669,7 +689,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, TMEM_COLS);
+        tmem_dealloc(tmem, G::TMEM_COLS);
     }
 }
 
@@ -680,10 +700,12 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
 // memory at the end.  S may exceed one GPU's split count (records gathered from other GPUs).
 constexpr int CMB_THREADS = 256;
 
-// ph = head h's record of the first split; records are ss floats apart.
+// Records of latent width R (o[R], m, l, 2 pad).  ph = head h's record of the first split;
+// records are ss floats apart; blockIdx.y selects 128 of the R columns.
 // record_out == 0: out[d] = merged, normalised attention (out = the head's output row).
 // record_out != 0: out = the head's record [kPartStride]: the merged, unnormalised record
 // (o = sum a_s o_s, m = m*, l = sum a_s l_s) -- the form that is exchanged between GPUs.
+template <int R>
 __device__ __forceinline__ void merge_head(const float* __restrict__ ph, int S, size_t ss,
                                            float* __restrict__ out, int record_out,
                                            float* s_alpha) {
@@ -693,7 +715,7 @@ __device__ __forceinline__ void merge_head(const float* __restrict__ ph, int S, 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     float m = -INFINITY;
-    for (int s = tid; s < S; s += CMB_THREADS) m = fmaxf(m, __ldg(ph + s * ss + kPartM));
+    for (int s = tid; s < S; s += CMB_THREADS) m = fmaxf(m, __ldg(ph + s * ss + R));
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
     if (lane == 0) s_m[warp] = m;
@@ -704,10 +726,10 @@ __device__ __forceinline__ void merge_head(const float* __restrict__ ph, int S, 
 
     float lsum = 0.0f;
     for (int s = tid; s < S; s += CMB_THREADS) {
-        const float ms = __ldg(ph + s * ss + kPartM);
+        const float ms = __ldg(ph + s * ss + R);
         const float a = (ms > -INFINITY) ? exp2f(ms - mstar) : 0.0f;
         s_alpha[s] = a;
-        lsum += a * __ldg(ph + s * ss + kPartL);
+        lsum += a * __ldg(ph + s * ss + (R + 1));
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
@@ -737,10 +759,10 @@ __device__ __forceinline__ void merge_head(const float* __restrict__ ph, int S, 
         if (record_out) {
             out[d0 + tid] = o;
             if (blockIdx.y == 0 && tid == 0) {
-                out[kPartM] = mstar;
-                out[kPartL] = l;
-                out[kPartL + 1] = 0.0f;
-                out[kPartL + 2] = 0.0f;
+                out[R] = mstar;
+                out[(R + 1)] = l;
+                out[R + 2] = 0.0f;
+                out[R + 3] = 0.0f;
             }
         } else {
             out[d0 + tid] = (mstar > -INFINITY) ? o / l : 0.0f;
@@ -748,22 +770,24 @@ __device__ __forceinline__ void merge_head(const float* __restrict__ ph, int S, 
     }
 }
 
-// grid (32 heads, 4 blocks of 128 columns).  record_out: see merge_head; out_hs = the output's
-// head stride in floats (kPartStride for records).
+// grid (32 heads, R / 128 blocks of 128 columns).  record_out: see merge_head; out_hs = the
+// output's head stride in floats (R + 4 for records).
+template <int R>
 __global__ void __launch_bounds__(CMB_THREADS)
 kqkv_combine_kernel(const float* __restrict__ part, int S, float* __restrict__ out, int64_t out_hs,
                     int record_out) {
     extern __shared__ float s_alpha[];   // [S]
     pdl_wait();
     const int h = blockIdx.x;
-    merge_head(part + static_cast<size_t>(h) * kPartStride, S,
-               static_cast<size_t>(H) * kPartStride, out + h * out_hs, record_out, s_alpha);
+    merge_head<R>(part + static_cast<size_t>(h) * (R + 4), S, static_cast<size_t>(H) * (R + 4),
+                  out + h * out_hs, record_out, s_alpha);
 }
 
-// Ragged batch: grid (32 heads, 4 column blocks, n_seq tokens).  Token t's window covers tiles
+// Ragged batch: grid (32 heads, R / 128 column blocks, n_seq tokens).  Token t's window covers tiles
 // [ps, ps + ts) of the concatenation; the CTAs owning them wrote their records for t at slots
 // c + t (kqkv_partial_kernel), so the records to merge are the contiguous slots
 // [c_first + t, c_last + t].  An empty window gives 0 (m4-kqkv.cu:337).
+template <int R>
 __global__ void __launch_bounds__(CMB_THREADS)
 kqkv_ragged_combine_kernel(const float* __restrict__ part, const int32_t* __restrict__ seq_base,
                            const int32_t* __restrict__ seq_len, int n_seq, int n_rows, int G,
@@ -794,27 +818,21 @@ kqkv_ragged_combine_kernel(const float* __restrict__ part, const int32_t* __rest
         if (threadIdx.x < 128) orow[blockIdx.y * 128 + threadIdx.x] = 0.0f;
         return;
     }
-    const size_t ss = static_cast<size_t>(H) * kPartStride;
-    merge_head(part + static_cast<size_t>(s_first + t) * ss + static_cast<size_t>(h) * kPartStride,
-               s_count, ss, orow, 0, s_alpha);
+    const size_t ss = static_cast<size_t>(H) * (R + 4);
+    merge_head<R>(part + static_cast<size_t>(s_first + t) * ss + static_cast<size_t>(h) * (R + 4),
+                  s_count, ss, orow, 0, s_alpha);
 }
 
 }  // namespace kq
 
-cudaError_t launch_kqkv_partials(const KqkvLaunch& a, cudaStream_t stream) {
+namespace {
+
+template <class G>
+cudaError_t launch_partials_geo(const KqkvLaunch& a, PFN_cuTensorMapEncodeTiled_v12000 encode,
+                                cudaStream_t stream) {
     using namespace kq;
-    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-    if (encode == nullptr) {
-        cudaDriverEntryPointQueryResult qres;
-        void* fn = nullptr;
-        cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
-                                                         cudaEnableDefault, &qres);
-        if (e != cudaSuccess || qres != cudaDriverEntryPointSuccess || fn == nullptr)
-            return note(e != cudaSuccess ? e : cudaErrorNotSupported);
-        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }
     CUtensorMap tmap;
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kKRow), static_cast<cuuint64_t>(a.n_kv)};
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(G::D), static_cast<cuuint64_t>(a.n_kv)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.kcache_row_bytes)};
     const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(TK)};
     const cuuint32_t estr[2] = {1, 1};
@@ -824,13 +842,13 @@ cudaError_t launch_kqkv_partials(const KqkvLaunch& a, cudaStream_t stream) {
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return note(cudaErrorInvalidValue);
 
-    static uint64_t attr_set = 0;   // one bit per device ordinal
+    static uint64_t attr_set = 0;   // one bit per device ordinal, per geometry instance
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess) return note(e);
     if (dev >= 64 || !((attr_set >> dev) & 1)) {
-        e = cudaFuncSetAttribute(kqkv_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 SMEM_BYTES);
+        e = cudaFuncSetAttribute(kqkv_partial_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 G::SMEM_BYTES);
         if (e != cudaSuccess) return note(e);
         if (dev < 64) attr_set |= 1ull << dev;
     }
@@ -846,33 +864,62 @@ cudaError_t launch_kqkv_partials(const KqkvLaunch& a, cudaStream_t stream) {
     p.seq_base = a.seq_base;
     p.seq_len = a.seq_len;
     p.n_seq = a.n_seq;
-    return launch(kqkv_partial_kernel, dim3(a.splits), dim3(NTHREADS), SMEM_BYTES, stream, a.flags,
-                  tmap, p);
+    return launch(kqkv_partial_kernel<G>, dim3(a.splits), dim3(NTHREADS), G::SMEM_BYTES, stream,
+                  a.flags, tmap, p);
 }
 
-cudaError_t launch_kqkv_combine(const float* part, int S, float* out, int64_t out_hs,
+}  // namespace
+
+cudaError_t launch_kqkv_partials(const KqkvLaunch& a, cudaStream_t stream) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (encode == nullptr) {
+        cudaDriverEntryPointQueryResult qres;
+        void* fn = nullptr;
+        cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
+                                                         cudaEnableDefault, &qres);
+        if (e != cudaSuccess || qres != cudaDriverEntryPointSuccess || fn == nullptr)
+            return note(e != cudaSuccess ? e : cudaErrorNotSupported);
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    if (a.latent == kq::GeoMistral::R) return launch_partials_geo<kq::GeoMistral>(a, encode, stream);
+    if (a.latent == kq::GeoBase::R) return launch_partials_geo<kq::GeoBase>(a, encode, stream);
+    return note(cudaErrorInvalidValue);
+}
+
+cudaError_t launch_kqkv_combine(const float* part, int S, int latent, float* out, int64_t out_hs,
                                 uint32_t flags, cudaStream_t stream) {
     const size_t smem = static_cast<size_t>(S) * sizeof(float);
-    if (smem > 48 * 1024) return cudaErrorInvalidValue;   // > 12288 records: not a real config
-    return launch(kq::kqkv_combine_kernel, dim3(kHeads, kLatent / 128), dim3(kq::CMB_THREADS), smem,
-                  stream, flags, part, S, out, out_hs, 0);
+    if (smem > 48 * 1024) return note(cudaErrorInvalidValue);   // > 12288 records: not a config
+    if (latent == 256)
+        return launch(kq::kqkv_combine_kernel<256>, dim3(kHeads, 2), dim3(kq::CMB_THREADS), smem,
+                      stream, flags, part, S, out, out_hs, 0);
+    return launch(kq::kqkv_combine_kernel<kLatent>, dim3(kHeads, kLatent / 128),
+                  dim3(kq::CMB_THREADS), smem, stream, flags, part, S, out, out_hs, 0);
 }
 
 cudaError_t launch_kqkv_ragged_combine(const float* part, const int32_t* seq_base,
                                        const int32_t* seq_len, int n_seq, int64_t n_rows,
-                                       int splits, float* out, int64_t out_hs, int64_t out_ts,
-                                       uint32_t flags, cudaStream_t stream) {
-    return launch(kq::kqkv_ragged_combine_kernel, dim3(kHeads, kLatent / 128, n_seq),
+                                       int splits, int latent, float* out, int64_t out_hs,
+                                       int64_t out_ts, uint32_t flags, cudaStream_t stream) {
+    if (latent == 256)
+        return launch(kq::kqkv_ragged_combine_kernel<256>, dim3(kHeads, 2, n_seq),
+                      dim3(kq::CMB_THREADS), 0, stream, flags, part, seq_base, seq_len, n_seq,
+                      static_cast<int>(n_rows), splits, out, out_hs, out_ts);
+    return launch(kq::kqkv_ragged_combine_kernel<kLatent>, dim3(kHeads, kLatent / 128, n_seq),
                   dim3(kq::CMB_THREADS), 0, stream, flags, part, seq_base, seq_len, n_seq,
                   static_cast<int>(n_rows), splits, out, out_hs, out_ts);
 }
 
-cudaError_t launch_kqkv_merge_records(const float* part, int S, float* out_records, uint32_t flags,
-                                      cudaStream_t stream) {
+cudaError_t launch_kqkv_merge_records(const float* part, int S, int latent, float* out_records,
+                                      uint32_t flags, cudaStream_t stream) {
     const size_t smem = static_cast<size_t>(S) * sizeof(float);
-    if (smem > 48 * 1024) return cudaErrorInvalidValue;
-    return launch(kq::kqkv_combine_kernel, dim3(kHeads, kLatent / 128), dim3(kq::CMB_THREADS), smem,
-                  stream, flags, part, S, out_records, static_cast<int64_t>(kPartStride), 1);
+    if (smem > 48 * 1024) return note(cudaErrorInvalidValue);
+    if (latent == 256)
+        return launch(kq::kqkv_combine_kernel<256>, dim3(kHeads, 2), dim3(kq::CMB_THREADS), smem,
+                      stream, flags, part, S, out_records, static_cast<int64_t>(256 + 4), 1);
+    return launch(kq::kqkv_combine_kernel<kLatent>, dim3(kHeads, kLatent / 128),
+                  dim3(kq::CMB_THREADS), smem, stream, flags, part, S, out_records,
+                  static_cast<int64_t>(kPartStride), 1);
 }
 
 }  // namespace m4b

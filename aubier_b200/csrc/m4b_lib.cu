@@ -3,6 +3,7 @@
 // relocatable device code.
 #include "m4b_kqkv.cu"
 #include "m4b_gemv.cu"
+#include "m4b_q8.cu"
 #include "m4b_api.cu"
 #include "m4b_noalloc.cu"
 #include "m4b_exchange.cu"

@@ -21,7 +21,7 @@
 namespace m4b {
 namespace noalloc {
 
-constexpr int kStaticRecords = kMaxSplits * kHeads;   // 148 splits x 32 heads, 2064 B each
+constexpr int kStaticRecords = kMaxSplits * kHeads;   // 148 splits x 32 heads, up to 2064 B each
 
 static __device__ __align__(256) float g_kqkv_static_part[kStaticRecords * kPartStride];
 
@@ -33,7 +33,8 @@ float* g_addr[64] = {};   // cached device address of the array, per device ordi
 extern "C" M4B_API int m4b_kqkv_static_scratch(const m4b_kqkv_args* a, m4b_stream_t stream) {
     using namespace m4b;
     if (!a) return M4B_EINVAL;
-    int rc = check_kqkv(*a);
+    int geom = 0;
+    int rc = check_kqkv(*a, &geom);
     if (rc != M4B_OK) return rc;
     int sms = 0;
     rc = device_check(&sms);
@@ -51,9 +52,9 @@ extern "C" M4B_API int m4b_kqkv_static_scratch(const m4b_kqkv_args* a, m4b_strea
     }
     float* part = noalloc::g_addr[dev];
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    cudaError_t e = launch_kqkv_partials(make_kqkv_launch(*a, splits, part), s);
+    cudaError_t e = launch_kqkv_partials(make_kqkv_launch(*a, geom, splits, part), s);
     if (e != cudaSuccess) return M4B_ECUDA;
-    e = launch_kqkv_combine(part, splits, static_cast<float*>(a->dst.data),
+    e = launch_kqkv_combine(part, splits, kGeo[geom].latent, static_cast<float*>(a->dst.data),
                             static_cast<int64_t>(a->dst.nb[2] / 4), a->flags & M4B_FLAG_PDL, s);
     return e == cudaSuccess ? M4B_OK : M4B_ECUDA;
 }

@@ -19,6 +19,7 @@ There is no fallback: if ``libm4b.so`` is missing, importing this module fails.
 from __future__ import annotations
 
 import ctypes
+import math
 import os
 from ctypes import c_float, c_int, c_int32, c_int64, c_uint32, c_uint64, c_void_p
 
@@ -29,6 +30,8 @@ LIB_PATH = os.path.join(_PKG, "libm4b.so")
 
 # geometry of the measured shape (BASELINE); engine/m1_layer.h:47-55 has the Mistral constants
 HEADS, NOPE, ROPE, LATENT, VHEAD = 32, 128, 64, 512, 128
+M_NOPE, M_LATENT = 64, 256   # the Mistral-Small-4 geometry (Q8_0 weights, KV row 320)
+Q8_BLOCK = 34                # ggml block_q8_0: f16 scale + 32 int8
 KROW = LATENT + ROPE
 PART_STRIDE = LATENT + 4   # o[512], m (log2 units), l, 2 pad
 TILE_KEYS = 128            # keys per KQKV tile: splits are balanced over ceil(N / 128) tiles
@@ -163,6 +166,26 @@ def _heads_desc(t: torch.Tensor, inner: int) -> Tensor:
     return gtensor(t, [inner, 1, t.shape[0], 1], [es, inner * es, hs, hs * t.shape[0]])
 
 
+def weight_desc(w: torch.Tensor) -> Tensor:
+    """A weight tensor: f16 (heads, rows, K) -> F16 [K, rows, heads]; uint8 Q8_0 bytes
+    (heads, rows, K / 32 * 34) or (rows, K / 32 * 34) -> Q8_0 [K, rows, heads]."""
+    if w.dtype == torch.uint8:
+        if w.shape[-1] % Q8_BLOCK or not w.is_contiguous():
+            raise M4Error(EINVAL, "Q8_0 weights: contiguous uint8 rows of 34-byte blocks")
+        K = w.shape[-1] // Q8_BLOCK * 32
+        rows = w.shape[-2]
+        heads = w.shape[0] if w.dim() == 3 else 1
+        row = w.shape[-1]
+        return gtensor(w, [K, rows, heads, 1], [Q8_BLOCK, row, row * rows, row * rows * heads],
+                       type_id=Q8_0)
+    return gtensor(w, list(reversed(w.shape)))
+
+
+def latent_of(kcache: torch.Tensor) -> int:
+    """The latent width R of a KV cache (rows of R + 64)."""
+    return kcache.shape[-1] - ROPE
+
+
 def _tokens_desc(t: torch.Tensor, inner: int, token_dim: int) -> Tensor:
     """ggml view of a (T, heads, >=inner) tensor with unit inner stride: [inner, heads, T] when
     token_dim == 2 (q, q_abs), [inner, T, heads] when token_dim == 1 (g_kqv, W_UV in/out)."""
@@ -205,11 +228,12 @@ def wkb(w_uk: torch.Tensor, q_nope: torch.Tensor, out: torch.Tensor | None = Non
     q_nope f32 (32, 128) with any row stride; out f32 (32, 512), any row stride (may be a view
     of Qcur)."""
     _need_cuda("GGML_OP_M4_WKB", w_uk, q_nope, out)
+    R = w_uk.shape[1]
     if out is None:
-        shape = (HEADS, LATENT) if q_nope.dim() == 2 else (q_nope.shape[0], HEADS, LATENT)
+        shape = (HEADS, R) if q_nope.dim() == 2 else (q_nope.shape[0], HEADS, R)
         out = torch.empty(shape, device=w_uk.device, dtype=torch.float32)
     a = WkbArgs()
-    a.src0 = gtensor(w_uk, list(reversed(w_uk.shape)))
+    a.src0 = weight_desc(w_uk)
     if q_nope.dim() == 3:   # a batch of tokens (T, 32, 128) -> (T, 32, 512)
         a.src1 = _tokens_desc(q_nope, q_nope.shape[2], 2)
         a.dst = _tokens_desc(out, out.shape[2], 2)
@@ -221,8 +245,8 @@ def wkb(w_uk: torch.Tensor, q_nope: torch.Tensor, out: torch.Tensor | None = Non
     return out
 
 
-def kqkv_scratch_bytes(n_kv: int) -> int:
-    return int(_lib.m4b_kqkv_scratch_bytes(0, n_kv))
+def kqkv_scratch_bytes(n_kv: int, latent: int = LATENT) -> int:
+    return int(_lib.m4b_kqkv_scratch_bytes(0 if latent == LATENT else 1, n_kv))
 
 
 def default_splits(n_kv: int) -> int:
@@ -249,13 +273,14 @@ def kqkv(kcache: torch.Tensor, q: torch.Tensor, mask: torch.Tensor | None, kq_sc
     any 16-byte-multiple row stride; q f32 (32, 576); mask f32 (N,) of 0/-inf or None;
     out f32 (32, 512).  ``scratch``: a byte tensor of at least kqkv_scratch_bytes(N)."""
     _need_cuda("GGML_OP_M4_KQKV", kcache, q, mask, out, scratch)
+    R = latent_of(kcache)
     if out is None:
-        out = torch.empty(HEADS, LATENT, device=q.device, dtype=torch.float32)
+        out = torch.empty(HEADS, R, device=q.device, dtype=torch.float32)
     if scratch is None:
-        scratch = torch.empty(max(kqkv_scratch_bytes(kcache.shape[0]), 16), device=q.device,
+        scratch = torch.empty(max(kqkv_scratch_bytes(kcache.shape[0], R), 16), device=q.device,
                               dtype=torch.uint8)
     a = _kqkv_args(kcache, q, mask, kq_scale, flags)
-    a.dst = _heads_desc(out, LATENT)
+    a.dst = _heads_desc(out, R)
     a.scratch = scratch.data_ptr()
     a.scratch_bytes = scratch.numel() * scratch.element_size()
     _check(_lib.m4b_kqkv(ctypes.byref(a), _stream()), "m4b_kqkv")
@@ -265,13 +290,14 @@ def kqkv(kcache: torch.Tensor, q: torch.Tensor, mask: torch.Tensor | None, kq_sc
 def kqkv_partials(kcache: torch.Tensor, q: torch.Tensor, mask: torch.Tensor | None,
                   kq_scale: float, splits: int | None = None, out: torch.Tensor | None = None,
                   flags: int = 0) -> torch.Tensor:
-    """Split-K partial records (S, 32, 516): o[512], m (log2 units), l per (split, head)."""
+    """Split-K partial records (S, 32, R + 4): o[R], m (log2 units), l per (split, head)."""
     _need_cuda("GGML_OP_M4_KQKV", kcache, q, mask, out)
+    P = latent_of(kcache) + 4
     if out is None:
         s = splits if splits is not None else default_splits(kcache.shape[0])
-        out = torch.empty(s, HEADS, PART_STRIDE, device=q.device, dtype=torch.float32)
+        out = torch.empty(s, HEADS, P, device=q.device, dtype=torch.float32)
     a = _kqkv_args(kcache, q, mask, kq_scale, flags)
-    a.dst = gtensor(out, [PART_STRIDE, HEADS, out.shape[0], 1])
+    a.dst = gtensor(out, [P, HEADS, out.shape[0], 1])
     _check(_lib.m4b_kqkv_partials(ctypes.byref(a), _stream()), "m4b_kqkv_partials")
     return out
 
@@ -288,8 +314,9 @@ def kqkv_ragged(kcache: torch.Tensor, q: torch.Tensor, seq_base: torch.Tensor,
     seq_base / seq_len int32 (T,) on the device; out f32 (T, 32, 512)."""
     _need_cuda("m4b_kqkv_ragged", kcache, q, seq_base, seq_len, out, scratch)
     T = q.shape[0]
+    R = latent_of(kcache)
     if out is None:
-        out = torch.empty(T, HEADS, LATENT, device=q.device, dtype=torch.float32)
+        out = torch.empty(T, HEADS, R, device=q.device, dtype=torch.float32)
     if scratch is None:
         scratch = torch.empty(max(kqkv_ragged_scratch_bytes(T), 16), device=q.device,
                               dtype=torch.uint8)
@@ -300,7 +327,7 @@ def kqkv_ragged(kcache: torch.Tensor, q: torch.Tensor, seq_base: torch.Tensor,
         if t.dtype != torch.int32 or t.dim() != 1 or t.stride(0) != 1:
             raise M4Error(EINVAL, f"{name} must be a contiguous 1-D int32 tensor")
         setattr(a, name, gtensor(t, [t.shape[0], 1, 1, 1]))
-    a.dst = _tokens_desc(out, LATENT, 1)
+    a.dst = _tokens_desc(out, R, 1)
     a.kq_scale = float(kq_scale)
     a.flags = flags
     a.scratch = scratch.data_ptr()
@@ -325,47 +352,95 @@ def _phase(phase: int, srcs, dst: Tensor, flags: int, scratch=None) -> None:
 
 def phase_wvb(w_uv: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = None,
               flags: int = 0) -> torch.Tensor:
-    """GGML_OP_M4_PHASE selector 1: out[h] = W_UV[h] . x[h].  w_uv f16 (32, 128, 512);
-    x f32 (32, 512) (any row stride); out f32 (32, 128)."""
+    """GGML_OP_M4_PHASE selector 1: out[h] = W_UV[h] . x[h].  w_uv f16 (32, 128, 512) or Q8_0
+    bytes (32, 128, 272); x f32 (32, R) (any row stride) or a token batch (T, 32, R);
+    out f32 (32, 128) / (T, 32, 128)."""
     _need_cuda("GGML_OP_M4_PHASE", w_uv, x, out)
+    R = x.shape[-1]
     if out is None:
         shape = (HEADS, VHEAD) if x.dim() == 2 else (x.shape[0], HEADS, VHEAD)
         out = torch.empty(shape, device=x.device, dtype=torch.float32)
-    if x.dim() == 3:   # a batch of tokens (T, 32, 512) -> (T, 32, 128)
-        xd, od = _tokens_desc(x, LATENT, 1), _tokens_desc(out, VHEAD, 1)
+    if x.dim() == 3:   # a batch of tokens (T, 32, R) -> (T, 32, 128)
+        xd, od = _tokens_desc(x, R, 1), _tokens_desc(out, VHEAD, 1)
     else:
-        xd, od = _heads_desc(x, LATENT), _heads_desc(out, VHEAD)
-    _phase(PHASE_WVB, [gtensor(w_uv, list(reversed(w_uv.shape))), xd], od, flags)
+        xd, od = _heads_desc(x, R), _heads_desc(out, VHEAD)
+    _phase(PHASE_WVB, [weight_desc(w_uv), xd], od, flags)
     return out
 
 
 def phase_combine_wvb(w_uv: torch.Tensor, partials: torch.Tensor,
                       out: torch.Tensor | None = None, attn_out: torch.Tensor | None = None,
                       scratch: torch.Tensor | None = None, flags: int = 0) -> torch.Tensor:
-    """GGML_OP_M4_PHASE selector 2 (additive): merge (S, 32, 516) partial records, then W_UV.
-    ``attn_out`` (32, 512) optionally receives the merged attention output."""
+    """GGML_OP_M4_PHASE selector 2 (additive): merge (S, 32, R + 4) partial records, then W_UV.
+    ``attn_out`` (32, R) optionally receives the merged attention output."""
     _need_cuda("GGML_OP_M4_PHASE", w_uv, partials, out, attn_out, scratch)
+    P = partials.shape[-1]
     if out is None:
         out = torch.empty(HEADS, VHEAD, device=partials.device, dtype=torch.float32)
     if attn_out is None and scratch is None:
         scratch = torch.empty(int(_lib.m4b_phase_scratch_bytes(2)), device=partials.device,
                               dtype=torch.uint8)
-    srcs = [gtensor(w_uv, list(reversed(w_uv.shape))),
-            gtensor(partials, [PART_STRIDE, HEADS, partials.shape[0], 1]),
-            _heads_desc(attn_out, LATENT) if attn_out is not None else None]
+    srcs = [weight_desc(w_uv), gtensor(partials, [P, HEADS, partials.shape[0], 1]),
+            _heads_desc(attn_out, P - 4) if attn_out is not None else None]
     _phase(PHASE_COMBINE_WVB, srcs, _heads_desc(out, VHEAD), flags, scratch)
     return out
 
 
 def phase_merge_records(partials: torch.Tensor, out: torch.Tensor | None = None,
                         flags: int = 0) -> torch.Tensor:
-    """GGML_OP_M4_PHASE selector 3 (additive): merge (S, 32, 516) partial records into one
-    unnormalised record per head, (1, 32, 516) -- the payload of the multi-GPU exchange."""
+    """GGML_OP_M4_PHASE selector 3 (additive): merge (S, 32, R + 4) partial records into one
+    unnormalised record per head, (1, 32, R + 4) -- the payload of the multi-GPU exchange."""
     _need_cuda("GGML_OP_M4_PHASE", partials, out)
+    P = partials.shape[-1]
     if out is None:
-        out = torch.empty(1, HEADS, PART_STRIDE, device=partials.device, dtype=torch.float32)
-    srcs = [None, gtensor(partials, [PART_STRIDE, HEADS, partials.shape[0], 1])]
-    _phase(PHASE_MERGE, srcs, gtensor(out, [PART_STRIDE, HEADS, 1, 1]), flags)
+        out = torch.empty(1, HEADS, P, device=partials.device, dtype=torch.float32)
+    srcs = [None, gtensor(partials, [P, HEADS, partials.shape[0], 1])]
+    _phase(PHASE_MERGE, srcs, gtensor(out, [P, HEADS, 1, 1]), flags)
+    return out
+
+
+def _f32_bits(x: float) -> int:
+    import struct
+    return struct.unpack("<i", struct.pack("<f", float(x)))[0]
+
+
+# the engine's attention scalars for the Mistral-Small-4 geometry (engine/m1_layer.cpp:60-95,
+# m1_layer.h:56-67): YaRN factor 128 over an 8192 original context
+MISTRAL_ROPE = {"freq_base": 10000.0, "freq_scale": 1.0 / 128.0, "ext_factor": 1.0,
+                "attn_factor": 1.0 / (1.0 + 0.1 * math.log(128.0)), "beta_fast": 32.0,
+                "beta_slow": 1.0, "eps": 9.999999974752427e-07, "n_dims": 64,
+                "n_ctx_orig": 8192}
+
+
+def phase_kvwrite(cur: torch.Tensor, w_kva: torch.Tensor, norm_w: torch.Tensor,
+                  kcache: torch.Tensor, kidx: torch.Tensor, pos: torch.Tensor,
+                  rope: dict | None = None, out: torch.Tensor | None = None,
+                  flags: int = 0) -> torch.Tensor:
+    """GGML_OP_M4_PHASE selector 0, the KV-write (Mistral-Small-4 geometry): Kcur = norm(W_kva .
+    cur) with YaRN rope on the last 64 values, written as f16 into kcache row kidx[0] (in place).
+    cur f32 (4096,); w_kva Q8_0 bytes (320, 4352); norm_w f32 (256,); kcache f16 (N, 320);
+    kidx int64 (1,) and pos int32 (1,) on the device; rope: the rope / norm scalars (default the
+    engine's, MISTRAL_ROPE).  Returns Kcur f32 (320,)."""
+    _need_cuda("GGML_OP_M4_PHASE", cur, w_kva, norm_w, kcache, kidx, pos, out)
+    rp = dict(MISTRAL_ROPE, **(rope or {}))
+    if out is None:
+        out = torch.empty(320, device=cur.device, dtype=torch.float32)
+    a = PhaseArgs()
+    a.src[0] = gtensor(cur, [cur.shape[0], 1, 1, 1])
+    a.src[1] = weight_desc(w_kva)
+    a.src[2] = gtensor(norm_w, [norm_w.shape[0], 1, 1, 1])
+    a.src[3] = _rows_desc(kcache, kcache.shape[1], kcache.shape[0])
+    a.src[4] = gtensor(kidx, [1, 1, 1, 1])
+    a.src[5] = gtensor(pos, [1, 1, 1, 1])
+    a.dst = gtensor(out, [out.shape[0], 1, 1, 1])
+    a.op_params[0] = PHASE_KVWRITE
+    for i, k in enumerate(("freq_base", "freq_scale", "ext_factor", "attn_factor", "beta_fast",
+                           "beta_slow", "eps"), start=1):
+        a.op_params[i] = _f32_bits(rp[k])
+    a.op_params[8] = int(rp["n_dims"])
+    a.op_params[9] = int(rp["n_ctx_orig"])
+    a.flags = flags
+    _check(_lib.m4b_phase(ctypes.byref(a), _stream()), "m4b_phase(0)")
     return out
 
 

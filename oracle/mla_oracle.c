@@ -268,3 +268,257 @@ void orc_kqkv_exact(const f16_t * kc, int64_t N, int D, int R, const float * q, 
         free(w); free(acc);
     }
 }
+
+/* ============================================================================================
+ * The Mistral-Small-4 geometry (engine/m1_layer.h:47-55): Q8_0 weights, Q8 activations.
+ *
+ * ggml's Q8_0 block (ggml-common.h): an f16 scale d, then 32 int8 quants; value = d * q.
+ * Two activation quantizations matter:
+ *   CPU graph (the oracle): ggml-cpu's x86 quantize_row_q8_0 with AVX2 / AVX-512 (the build in
+ *     oracle/_ref): per 32 values amax; d = amax/127 stored as f16; multiplier 127/amax (0 for
+ *     an all-zero block); q = round-half-to-even(x * multiplier)
+ *     (ggml-cpu/arch/x86/quants.c:302-346).  The dot is sum_b f16(d_w) f16(d_x) sum_i q_w q_x
+ *     (vec_dot_q8_0_q8_0); summed here in double.
+ *   Fused reference kernels (MMVQ's Q8_1 form, the numerics GGML_OP_M4_* replicate): per 32
+ *     values amax; d = amax/127; the quants round half away from zero, either x / d
+ *     (m4-wkb.cu:36-47) or x * (1/d) (m4-phase.cu:69-74 and :107-116); the scale enters the dot
+ *     as f16(d).  Restated here with the association of those kernels, in float.
+ * ============================================================================================ */
+typedef struct {
+    f16_t d;
+    int8_t qs[32];
+} q8_block;   /* 34 bytes, the ggml layout */
+
+/* Weights: quantize rows of K floats (K % 32 == 0) to Q8_0 bytes with ggml's reference
+ * quantizer (scale amax/127, multiplier 1/d, roundf; ggml-quants.c quantize_row_q8_0_ref).
+ * Only used to make test weights; both sides of a comparison then read the same bytes. */
+void orc_q8_0_quantize(const float * x, int64_t rows, int K, uint8_t * out) {
+    const int nb = K / 32;
+    for (int64_t r = 0; r < rows; ++r) {
+        for (int b = 0; b < nb; ++b) {
+            const float * xb = x + (size_t) r * K + (size_t) b * 32;
+            q8_block blk;
+            float amax = 0.0f;
+            for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(xb[i]));
+            const float d = amax / 127.0f;
+            const float id = d != 0.0f ? 1.0f / d : 0.0f;
+            blk.d = f2h(d);
+            for (int i = 0; i < 32; ++i) blk.qs[i] = (int8_t) roundf(xb[i] * id);
+            memcpy(out + ((size_t) r * nb + b) * 34, &blk, 34);
+        }
+    }
+}
+
+/* Activation block quantizers: q[32] and the f16-rounded scale the dot uses. */
+static void quant_cpu(const float * x, int8_t * q, float * d16) {
+    float amax = 0.0f;
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(x[i]));
+    *d16 = round_f16(amax / 127.0f);
+    const float mul = amax != 0.0f ? 127.0f / amax : 0.0f;
+    for (int i = 0; i < 32; ++i) q[i] = (int8_t) (int) nearbyintf(x[i] * mul);  /* ties to even */
+}
+
+/* mode 0: x / d (m4-wkb.cu), mode 1: x * (1/d) (m4-phase.cu) -- both round half away from zero */
+static void quant_fused(const float * x, int8_t * q, float * d16, int mode) {
+    float amax = 0.0f;
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(x[i]));
+    const float d = amax / 127.0f;
+    *d16 = round_f16(d);
+    const float id = d != 0.0f ? 1.0f / d : 0.0f;
+    for (int i = 0; i < 32; ++i) {
+        float v;
+        if (mode == 0) v = amax == 0.0f ? 0.0f : roundf(x[i] / d);
+        else v = roundf(x[i] * id);
+        q[i] = (int8_t) (int) v;
+    }
+}
+
+static inline const q8_block * q8_row(const uint8_t * w, int64_t row, int K) {
+    return (const q8_block *) (w + (size_t) row * (K / 32) * 34);
+}
+
+static inline int dot_i8(const int8_t * a, const int8_t * b) {
+    int s = 0;
+    for (int i = 0; i < 32; ++i) s += (int) a[i] * (int) b[i];
+    return s;
+}
+
+/*
+ * WKB with Q8_0 W_UK [H][R][K] (ggml [K, R, H]): out[h][r] = W_UK[h][r] . Q8(q[h][0:K]).
+ * numerics 0 = the CPU graph (mul_mat Q8_0, m1_layer.cpp:445); 1 = the fused reference kernel
+ * (m4-wkb.cu:21-53: acc over the blocks in order, acc += (d_w * f16(d_x)) * sum).
+ */
+void orc_wkb_q8(const uint8_t * w, const float * q, int64_t q_stride, int H, int R, int K,
+                float * out, int64_t out_stride, int numerics) {
+    const int nb = K / 32;
+    int8_t * xq = (int8_t *) malloc((size_t) K);
+    float * xd = (float *) malloc(sizeof(float) * (size_t) nb);
+    for (int h = 0; h < H; ++h) {
+        for (int b = 0; b < nb; ++b) {
+            const float * xb = q + (size_t) h * q_stride + (size_t) b * 32;
+            if (numerics == 0) quant_cpu(xb, xq + b * 32, xd + b);
+            else quant_fused(xb, xq + b * 32, xd + b, 0);
+        }
+        for (int r = 0; r < R; ++r) {
+            const q8_block * wr = q8_row(w, (int64_t) h * R + r, K);
+            if (numerics == 0) {
+                double acc = 0.0;
+                for (int b = 0; b < nb; ++b)
+                    acc += (double) (h2f(wr[b].d) * xd[b]) * (double) dot_i8(wr[b].qs, xq + b * 32);
+                out[(size_t) h * out_stride + r] = (float) acc;
+            } else {
+                float acc = 0.0f;
+                for (int b = 0; b < nb; ++b)
+                    acc += h2f(wr[b].d) * xd[b] * (float) dot_i8(wr[b].qs, xq + b * 32);
+                out[(size_t) h * out_stride + r] = acc;
+            }
+        }
+    }
+    free(xq);
+    free(xd);
+}
+
+/*
+ * W_UV with Q8_0 W_UV [H][V][R] (ggml [R, V, H]): out[h][j] = W_UV[h][j] . Q8(x[h][0:R]).
+ * numerics 0 = the CPU graph (mul_mat, m1_layer.cpp:502); 1 = the fused reference kernel
+ * (m4-phase.cu:52-89: lane l of a warp owns element l of every block, accumulates
+ * (d_w * f16(d_x)) * (q_w q_x) over the blocks, then a butterfly sum over the 32 lanes).
+ */
+void orc_wvb_q8(const uint8_t * w, const float * x, int64_t x_stride, int H, int V, int R,
+                float * out, int numerics) {
+    const int nb = R / 32;
+    int8_t * xq = (int8_t *) malloc((size_t) R);
+    float * xd = (float *) malloc(sizeof(float) * (size_t) nb);
+    for (int h = 0; h < H; ++h) {
+        for (int b = 0; b < nb; ++b) {
+            const float * xb = x + (size_t) h * x_stride + (size_t) b * 32;
+            if (numerics == 0) quant_cpu(xb, xq + b * 32, xd + b);
+            else quant_fused(xb, xq + b * 32, xd + b, 1);
+        }
+        for (int j = 0; j < V; ++j) {
+            const q8_block * wr = q8_row(w, (int64_t) h * V + j, R);
+            if (numerics == 0) {
+                double acc = 0.0;
+                for (int b = 0; b < nb; ++b)
+                    acc += (double) (h2f(wr[b].d) * xd[b]) * (double) dot_i8(wr[b].qs, xq + b * 32);
+                out[(size_t) h * V + j] = (float) acc;
+            } else {
+                float lane[32];
+                for (int l = 0; l < 32; ++l) {
+                    float a = 0.0f;
+                    for (int b = 0; b < nb; ++b)
+                        a += h2f(wr[b].d) * xd[b] *
+                             (float) ((int) wr[b].qs[l] * (int) xq[b * 32 + l]);
+                    lane[l] = a;
+                }
+                for (int off = 16; off > 0; off >>= 1) {
+                    float nx[32];
+                    for (int l = 0; l < 32; ++l) nx[l] = lane[l] + lane[l ^ off];
+                    memcpy(lane, nx, sizeof(lane));
+                }
+                out[(size_t) h * V + j] = lane[0];
+            }
+        }
+    }
+    free(xq);
+    free(xd);
+}
+
+/*
+ * YaRN correction dims (the published YaRN rule as ggml applies it, ggml.c:4630-4644): the
+ * rotary dims whose wavelength at the original context sits between beta_fast and beta_slow
+ * rotations: corr(b) = n_dims * ln(n_ctx_orig / (b * 2 pi)) / (2 ln(base)); the ramp runs from
+ * max(0, floor(corr(beta_fast))) to min(n_dims - 1, ceil(corr(beta_slow))).
+ */
+void orc_rope_corr_dims(int n_dims, int n_ctx_orig, float freq_base, float beta_fast,
+                        float beta_slow, float * dims) {
+    const float pi = 3.14159265358979323846f;
+    const float a = n_dims * logf(n_ctx_orig / (beta_fast * 2 * pi)) / (2 * logf(freq_base));
+    const float b = n_dims * logf(n_ctx_orig / (beta_slow * 2 * pi)) / (2 * logf(freq_base));
+    dims[0] = fmaxf(0.0f, floorf(a));
+    dims[1] = fminf((float) (n_dims - 1), ceilf(b));
+}
+
+/* one YaRN-scaled rotation angle and magnitude (ggml-cpu/ops.cpp:6179-6201 rope_yarn) */
+static void yarn_cos_sin(float theta_extrap, float freq_scale, const float * corr, int p,
+                         float ext_factor, float mscale, float * c, float * s) {
+    float theta = freq_scale * theta_extrap;
+    if (ext_factor != 0.0f) {
+        const float y = ((float) p - corr[0]) / fmaxf(0.001f, corr[1] - corr[0]);
+        const float mix = (1.0f - fminf(1.0f, fmaxf(0.0f, y))) * ext_factor;
+        theta = theta * (1.0f - mix) + theta_extrap * mix;
+        mscale *= 1.0f + 0.1f * logf(1.0f / freq_scale);
+    }
+    *c = cosf(theta) * mscale;
+    *s = sinf(theta) * mscale;
+}
+
+/*
+ * KV-write for one token (GGML_OP_M4_PHASE selector 0; the flag-OFF sequence of
+ * m1_layer.cpp:422-460): kv = W_kva . Q8(cur) [D = R + rope]; Kcur[0:R) = rms_norm(kv[0:R]) *
+ * norm_w; Kcur[R:D) = rope_yarn(kv[R:D], pos) in NORMAL mode (pairs (2p, 2p+1)); the cache row
+ * kidx receives f16(Kcur).
+ * numerics 0 = the CPU graph: Q8_0 activations as quant_cpu, the norm's sum of squares in
+ *   double (ops.cpp:4140-4147), the angle pos * theta_scale^p built by repeated multiplication
+ *   (ops.cpp:6203-6217);
+ * numerics 1 = the fused reference (m4-phase.cu:97-200): Q8_1 activations (x * 1/d), the sum of
+ *   squares in float over 10 warp partials then summed in order, the angle pos * powf(theta_scale, p).
+ * kcache: [N][D] f16, written at row kidx.  kcur: [D] f32 out.
+ */
+void orc_kvwrite(const float * cur, int n_in, const uint8_t * w, const float * norm_w, int R,
+                 int rope, f16_t * kcache, int64_t kidx, int pos, float eps, float freq_base,
+                 float freq_scale, float ext_factor, float attn_factor, float beta_fast,
+                 float beta_slow, int n_ctx_orig, int numerics, float * kcur) {
+    const int D = R + rope;
+    const int nb = n_in / 32;
+    int8_t * xq = (int8_t *) malloc((size_t) n_in);
+    float * xd = (float *) malloc(sizeof(float) * (size_t) nb);
+    for (int b = 0; b < nb; ++b) {
+        if (numerics == 0) quant_cpu(cur + (size_t) b * 32, xq + b * 32, xd + b);
+        else quant_fused(cur + (size_t) b * 32, xq + b * 32, xd + b, 1);
+    }
+    float * kv = (float *) malloc(sizeof(float) * (size_t) D);
+    for (int o = 0; o < D; ++o) {
+        const q8_block * wr = q8_row(w, o, n_in);
+        double acc = 0.0;
+        for (int b = 0; b < nb; ++b)
+            acc += (double) (h2f(wr[b].d) * xd[b]) * (double) dot_i8(wr[b].qs, xq + b * 32);
+        kv[o] = (float) acc;
+    }
+    /* RMS norm of [0, R) times the norm weight */
+    float scale;
+    if (numerics == 0) {
+        double ss = 0.0;
+        for (int i = 0; i < R; ++i) ss += (double) (kv[i] * kv[i]);
+        const float mean = (float) (ss / R);
+        scale = 1.0f / sqrtf(mean + eps);
+    } else {
+        float part[32] = {0};
+        const int nw = (D + 31) / 32;
+        for (int i = 0; i < R; ++i) part[i / 32] += kv[i] * kv[i];
+        float ssf = 0.0f;
+        for (int i = 0; i < nw; ++i) ssf += part[i];
+        scale = 1.0f / sqrtf(ssf / (float) R + eps);
+    }
+    for (int i = 0; i < R; ++i) kcur[i] = numerics == 0 ? (kv[i] * scale) * norm_w[i]
+                                                        : scale * kv[i] * norm_w[i];
+    /* rope of [R, D) */
+    float corr[2];
+    orc_rope_corr_dims(rope, n_ctx_orig, freq_base, beta_fast, beta_slow, corr);
+    const float theta_scale = powf(freq_base, -2.0f / (float) rope);
+    float theta_it = (float) pos;
+    for (int p = 0; p < rope / 2; ++p) {
+        const float te = numerics == 0 ? theta_it : (float) pos * powf(theta_scale, (float) p);
+        float c, s;
+        yarn_cos_sin(te, freq_scale, corr, p, ext_factor, attn_factor, &c, &s);
+        const float x0 = kv[R + 2 * p], x1 = kv[R + 2 * p + 1];
+        kcur[R + 2 * p] = x0 * c - x1 * s;
+        kcur[R + 2 * p + 1] = x0 * s + x1 * c;
+        theta_it *= theta_scale;
+    }
+    if (kcache)
+        for (int i = 0; i < D; ++i) kcache[(size_t) kidx * D + i] = f2h(kcur[i]);
+    free(xq);
+    free(xd);
+    free(kv);
+}

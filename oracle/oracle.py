@@ -55,6 +55,14 @@ def lib():
         _lib.orc_kqkv_partial.argtypes = [_u16p, i64, i64, c_int, c_int, _f32p, i64, c_int, _f32p,
                                           c_float, _f32p]
         _lib.orc_combine.argtypes = [_f32p, c_int, c_int, c_int, _f32p]
+        u8p = ctypes.POINTER(ctypes.c_uint8)
+        _lib.orc_q8_0_quantize.argtypes = [_f32p, i64, c_int, u8p]
+        _lib.orc_wkb_q8.argtypes = [u8p, _f32p, i64, c_int, c_int, c_int, _f32p, i64, c_int]
+        _lib.orc_wvb_q8.argtypes = [u8p, _f32p, i64, c_int, c_int, c_int, _f32p, c_int]
+        _lib.orc_rope_corr_dims.argtypes = [c_int, c_int, c_float, c_float, c_float, _f32p]
+        _lib.orc_kvwrite.argtypes = [_f32p, c_int, u8p, _f32p, c_int, c_int, _u16p, i64, c_int,
+                                     c_float, c_float, c_float, c_float, c_float, c_float,
+                                     c_float, c_int, c_int, _f32p]
     return _lib
 
 
@@ -69,6 +77,86 @@ def _f16(a):
         a = a.view(np.float16)
     a = np.ascontiguousarray(a, dtype=np.float16)
     return a, a.ctypes.data_as(_u16p)
+
+
+# ---------------------------------------------------------------------------------------------
+# Q8_0 weights (the Mistral-Small-4 geometry).  numerics: CPU = the unfused CPU graph (the
+# oracle), FUSED = the reference's fused kernels (MMVQ's Q8_1 activation form).
+# ---------------------------------------------------------------------------------------------
+CPU, FUSED = 0, 1
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+
+
+def _u8(a):
+    a = np.ascontiguousarray(a, dtype=np.uint8)
+    return a, a.ctypes.data_as(_u8p)
+
+
+def q8_0_quantize(w: np.ndarray) -> np.ndarray:
+    """Float rows (..., K) -> Q8_0 bytes (..., K // 32 * 34), ggml's reference quantizer."""
+    w32, wp = _f32(w)
+    K = w32.shape[-1]
+    rows = w32.size // K
+    out = np.empty(w32.shape[:-1] + (K // 32 * 34,), np.uint8)
+    lib().orc_q8_0_quantize(wp, rows, K, out.ctypes.data_as(_u8p))
+    return out
+
+
+def q8_0_dequantize(wq: np.ndarray, K: int) -> np.ndarray:
+    """Q8_0 bytes (..., K // 32 * 34) -> float32 (..., K)."""
+    b = np.ascontiguousarray(wq).reshape(-1, 34)
+    d = b[:, :2].copy().view(np.float16).astype(np.float32)
+    q = b[:, 2:].view(np.int8).astype(np.float32)
+    return (d * q).reshape(wq.shape[:-1] + (K,))
+
+
+def wkb_q8(w_uk_q8: np.ndarray, q: np.ndarray, nope: int, R: int, numerics: int = CPU) -> np.ndarray:
+    """q_abs[h] = W_UK[h] . Q8(q[h, :nope]).  w_uk_q8 Q8_0 bytes (H, R, nope/32*34)."""
+    H = q.shape[0]
+    w, wp = _u8(w_uk_q8)
+    qq, qp = _f32(q)
+    out = np.empty((H, R), np.float32)
+    lib().orc_wkb_q8(wp, qp, qq.shape[1], H, R, nope, out.ctypes.data_as(_f32p), R, numerics)
+    return out
+
+
+def wvb_q8(w_uv_q8: np.ndarray, x: np.ndarray, V: int, numerics: int = CPU) -> np.ndarray:
+    """out[h] = W_UV[h] . Q8(x[h]).  w_uv_q8 Q8_0 bytes (H, V, R/32*34); x f32 (H, R)."""
+    H, R = x.shape
+    w, wp = _u8(w_uv_q8)
+    xx, xp = _f32(x)
+    out = np.empty((H, V), np.float32)
+    lib().orc_wvb_q8(wp, xp, xx.shape[1], H, V, R, out.ctypes.data_as(_f32p), numerics)
+    return out
+
+
+def rope_corr_dims(n_dims, n_ctx_orig, freq_base, beta_fast, beta_slow):
+    d = np.zeros(2, np.float32)
+    lib().orc_rope_corr_dims(n_dims, n_ctx_orig, freq_base, beta_fast, beta_slow,
+                             d.ctypes.data_as(_f32p))
+    return d
+
+
+def kvwrite(cur, w_q8, norm_w, kcache, kidx, pos, rp, numerics: int = CPU):
+    """Selector-0 KV-write for one token.  cur f32 (n_in,); w_q8 Q8_0 bytes (D, n_in/32*34);
+    norm_w f32 (R,); kcache f16 (N, D), updated in place at row kidx (None: no cache);
+    rp: dict eps, freq_base, freq_scale, ext_factor, attn_factor, beta_fast, beta_slow, n_dims,
+    n_ctx_orig.  Returns Kcur f32 (D,)."""
+    cc, cp = _f32(cur)
+    w, wp = _u8(w_q8)
+    nw, np_ = _f32(norm_w)
+    R = nw.shape[0]
+    D = w.shape[0]
+    kcur = np.empty(D, np.float32)
+    kc_ptr = None
+    if kcache is not None:
+        assert kcache.dtype == np.float16 and kcache.flags.c_contiguous
+        kc_ptr = kcache.ctypes.data_as(_u16p)
+    lib().orc_kvwrite(cp, cc.shape[0], wp, np_, R, D - R, kc_ptr, int(kidx), int(pos),
+                      rp["eps"], rp["freq_base"], rp["freq_scale"], rp["ext_factor"],
+                      rp["attn_factor"], rp["beta_fast"], rp["beta_slow"], int(rp["n_ctx_orig"]),
+                      numerics, kcur.ctypes.data_as(_f32p))
+    return kcur
 
 
 def wkb(w_uk: np.ndarray, q: np.ndarray, nope: int) -> np.ndarray:
@@ -180,7 +268,18 @@ def ref_lib():
         _ref.ref_mla_create.argtypes = [ctypes.c_int] * 5 + [ctypes.c_int64, ctypes.c_float,
                                                              ctypes.c_int]
         _ref.ref_mla_destroy.argtypes = [vp]
-        _ref.ref_mla_set_inputs.argtypes = [vp, _f32p, _u16p, _u16p, _f32p, _u16p]
+        _ref.ref_mla_create_typed.restype = vp
+        _ref.ref_mla_create_typed.argtypes = _ref.ref_mla_create.argtypes + [ctypes.c_int]
+        _ref.ref_mla_set_inputs.argtypes = [vp, _f32p, vp, _u16p, _f32p, vp]
+        cf, ci = ctypes.c_float, ctypes.c_int
+        _ref.ref_kvw_create.restype = vp
+        _ref.ref_kvw_create.argtypes = [ci, ci, ci, ctypes.c_int64] + [cf] * 7 + [ci, ci]
+        _ref.ref_kvw_set_inputs.argtypes = [vp, _f32p, vp, _f32p, _u16p, ctypes.c_int64,
+                                            ctypes.c_int32]
+        _ref.ref_kvw_compute.argtypes = [vp]
+        _ref.ref_kvw_compute.restype = ctypes.c_int
+        _ref.ref_kvw_get_outputs.argtypes = [vp, _f32p, _u16p]
+        _ref.ref_kvw_destroy.argtypes = [vp]
         _ref.ref_mla_compute.argtypes = [vp]
         _ref.ref_mla_compute.restype = ctypes.c_int
         _ref.ref_mla_get_outputs.argtypes = [vp, _f32p, _f32p, _f32p, _f32p]
@@ -192,22 +291,30 @@ def ref_lib():
 class RefMLA:
     """The reference's unfused MLA decode graph on its own ggml-cpu backend (built once)."""
 
-    def __init__(self, H, nope, rope, R, V, N, scale, n_threads=None):
+    GGML_F16, GGML_Q8_0 = 1, 8
+
+    def __init__(self, H, nope, rope, R, V, N, scale, n_threads=None, weights="f16"):
+        """weights: "f16" (BASELINE) or "q8_0" (the Mistral-Small-4 geometry; w_uk / w_uv are
+        then passed as Q8_0 bytes)."""
         self.H, self.nope, self.rope, self.R, self.V, self.N = H, nope, rope, R, V, N
         self.n_threads = n_threads or os.cpu_count() or 1
-        self._h = ref_lib().ref_mla_create(H, nope, rope, R, V, N, float(scale), self.n_threads)
+        self.q8 = weights == "q8_0"
+        wt = self.GGML_Q8_0 if self.q8 else self.GGML_F16
+        self._h = ref_lib().ref_mla_create_typed(H, nope, rope, R, V, N, float(scale),
+                                                 self.n_threads, wt)
         if not self._h:
             raise RuntimeError("ref_mla_create failed")
         self._keep = []
 
     def set_inputs(self, q=None, w_uk=None, kc=None, mask=None, w_uv=None):
-        args, keep = [], []
-        for a, conv in ((q, _f32), (w_uk, _f16), (kc, _f16), (mask, _f32), (w_uv, _f16)):
+        wconv = _u8 if self.q8 else _f16
+        keep, args = [], []
+        for a, conv in ((q, _f32), (w_uk, wconv), (kc, _f16), (mask, _f32), (w_uv, wconv)):
             if a is None:
                 args.append(None)
             else:
                 arr, ptr = conv(a)
-                keep.append(arr)
+                keep.append(arr)        # alive until the copy below has run
                 args.append(ptr)
         ref_lib().ref_mla_set_inputs(self._h, *args)
 
@@ -233,6 +340,48 @@ class RefMLA:
     def close(self):
         if self._h:
             ref_lib().ref_mla_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class RefKVWrite:
+    """The reference's unfused KV-write sequence (m1_layer.cpp:422-460) on its own ggml-cpu."""
+
+    def __init__(self, n_in, R, rope, N, rp, n_threads=None):
+        self.n_in, self.R, self.rope, self.N = n_in, R, rope, N
+        self.D = R + rope
+        self._h = ref_lib().ref_kvw_create(n_in, R, rope, N, rp["eps"], rp["freq_base"],
+                                           rp["freq_scale"], rp["ext_factor"], rp["attn_factor"],
+                                           rp["beta_fast"], rp["beta_slow"], int(rp["n_ctx_orig"]),
+                                           n_threads or os.cpu_count() or 1)
+        if not self._h:
+            raise RuntimeError("ref_kvw_create failed")
+
+    def run(self, cur, w_q8, norm_w, kcache, kidx, pos):
+        """Returns (Kcur f32 (D,), the cache f16 (N, D) after the write)."""
+        c, cp = _f32(cur)
+        w, wp = _u8(w_q8)
+        nw, nwp = _f32(norm_w)
+        kc, kcp = _f16(kcache)
+        ref_lib().ref_kvw_set_inputs(self._h, cp, ctypes.cast(wp, ctypes.c_void_p), nwp, kcp,
+                                     int(kidx), int(pos))
+        rc = ref_lib().ref_kvw_compute(self._h)
+        if rc != 0:
+            raise RuntimeError(f"ggml_graph_compute returned {rc}")
+        kcur = np.empty(self.D, np.float32)
+        out = np.empty((self.N, self.D), np.float16)
+        ref_lib().ref_kvw_get_outputs(self._h, kcur.ctypes.data_as(_f32p),
+                                      out.ctypes.data_as(_u16p))
+        return kcur, out
+
+    def close(self):
+        if self._h:
+            ref_lib().ref_kvw_destroy(self._h)
             self._h = None
 
     def __del__(self):

@@ -103,3 +103,37 @@ def packed_bases(lengths, gap: int = 0) -> np.ndarray:
     ``gap`` unused rows after each)."""
     lengths = np.asarray(lengths, np.int64)
     return np.concatenate([[0], np.cumsum(lengths + gap)[:-1]]).astype(np.int64)
+
+
+# The Mistral-Small-4 geometry (engine/m1_layer.h:47-55): nope 64, rope 64, latent 256, KV row
+# 320, Q8_0 W_UK / W_UV.  Weights are drawn like BASELINE's (N(0, 0.02)) and stored as Q8_0 with
+# ggml's reference quantizer, so every consumer reads the same bytes.
+MISTRAL = Geometry(nope=64, rope=64, R=256, V=128)
+
+# the engine's rope / norm scalars for that geometry (m1_layer.cpp:60-95, m1_layer.h:56-67)
+MISTRAL_ROPE = {"freq_base": 10000.0, "freq_scale": 1.0 / 128.0, "ext_factor": 1.0,
+                "attn_factor": 1.0 / (1.0 + 0.1 * math.log(128.0)), "beta_fast": 32.0,
+                "beta_slow": 1.0, "eps": 9.999999974752427e-07, "n_dims": 64, "n_ctx_orig": 8192}
+
+
+def make_layer_q8(seed: int, N: int, g: Geometry = MISTRAL):
+    """(q f32 (H, dq), W_UK Q8_0 bytes (H, R, nope/32*34), kcache f16 (N, D),
+    W_UV Q8_0 bytes (H, V, R/32*34))."""
+    from oracle import oracle as O
+    q = normal(seed * 8 + 1, g.H * g.dq).astype(np.float32).reshape(g.H, g.dq)
+    w_uk = (0.02 * normal(seed * 8 + 2, g.H * g.R * g.nope)).astype(np.float32).reshape(
+        g.H, g.R, g.nope)
+    kc = normal(seed * 8 + 3, N * g.D).astype(np.float16).reshape(N, g.D)
+    w_uv = (0.02 * normal(seed * 8 + 4, g.H * g.V * g.R)).astype(np.float32).reshape(
+        g.H, g.V, g.R)
+    return q, O.q8_0_quantize(w_uk), kc, O.q8_0_quantize(w_uv)
+
+
+def make_kvwrite(seed: int, N: int, n_in: int = 4096, g: Geometry = MISTRAL):
+    """(cur f32 (n_in,), W_kva Q8_0 bytes (D, n_in/32*34), kv_a_norm f32 (R,), kcache f16 (N, D))."""
+    from oracle import oracle as O
+    cur = normal(seed * 8 + 5, n_in).astype(np.float32)
+    w = (0.02 * normal(seed * 8 + 6, g.D * n_in)).astype(np.float32).reshape(g.D, n_in)
+    nw = (1.0 + 0.1 * normal(seed * 8 + 7, g.R)).astype(np.float32)
+    kc = normal(seed * 8 + 3, N * g.D).astype(np.float16).reshape(N, g.D)
+    return cur, O.q8_0_quantize(w), nw, kc

@@ -92,9 +92,51 @@ def test_supports_op_rejects_contract_violations():
     assert not m4.supports_op(m4.OP_KQKV, [unaligned, QCUR, MASK], ATTN)
     assert not m4.supports_op(m4.OP_WKB, [WUK, contiguous(m4.F32, [128, 16, 1, 1], 4)], QABS)
     assert not m4.supports_op(m4.OP_PHASE, [WUV, ATTN], OUT, [3] + [0] * 15)   # unknown phase
-    assert not m4.supports_op(m4.OP_PHASE, [WUV, ATTN], OUT, [0] + [0] * 15)   # kvwrite: Mistral
-    q8 = contiguous(m4.Q8_0, [64, 256, 32, 1], 1)                      # Mistral W_UK: not here yet
-    assert not m4.supports_op(m4.OP_WKB, [q8, QNOPE], QABS)
+    assert not m4.supports_op(m4.OP_PHASE, [WUV, ATTN], OUT, [0] + [0] * 15)   # kvwrite operands
+    assert not m4.supports_op(m4.OP_WKB, [Q8_WUK, QNOPE], QABS)        # Q8_0 W_UK, BASELINE q
+    assert not m4.supports_op(m4.OP_KQKV, [KC_M, QCUR, MASK_M], ATTN)  # mixed geometries
+    bad_kvw = _kvwrite_srcs()
+    bad_kvw[1] = contiguous(m4.Q8_0, [4096, 320, 1, 1], 34)            # ggml strides of Q8_0
+    bad_kvw[1].nb[0] = 32
+    assert not m4.supports_op(m4.OP_PHASE, bad_kvw, KCUR, KVW_PARAMS)
+    assert not m4.supports_op(m4.OP_PHASE, _kvwrite_srcs(), KCUR, [0] + [0] * 7 + [32, 8192] + [0] * 6)
+
+
+# Mistral-Small-4 geometry (engine/m1_layer.h:47-55): latent 256, row 320, Q8_0 weights
+def q8(ne):
+    """A packed Q8_0 tensor: ne[0] values per row in 34-byte blocks of 32."""
+    row = ne[0] // 32 * 34
+    return T(m4.Q8_0, ne, [34, row, row * ne[1], row * ne[1] * ne[2]])
+
+
+Q8_WUK = q8([64, 256, 32, 1])
+Q8_WUV = q8([256, 128, 32, 1])
+QNOPE_M = T(m4.F32, [64, 32, 1, 1], [4, 512, 512 * 32, 512 * 32])     # head stride 128 floats
+QABS_M = contiguous(m4.F32, [256, 32, 1, 1], 4)
+KC_M = contiguous(m4.F16, [320, N, 1, 1], 2)
+QCUR_M = contiguous(m4.F32, [320, 32, 1, 1], 4)
+MASK_M = MASK
+ATTN_M = T(m4.F32, [256, 1, 32, 1], [4, 1024, 1024, 1024 * 32])
+PARTS_M = contiguous(m4.F32, [260, 32, 7, 1], 4)
+KCUR = contiguous(m4.F32, [320, 1, 1, 1], 4)
+KVW_PARAMS = [0, 0, 0, 0, 0, 0, 0, 0, 64, 8192] + [0] * 6
+
+
+def _kvwrite_srcs():
+    return [contiguous(m4.F32, [4096, 1, 1, 1], 4), q8([4096, 320, 1, 1]),
+            contiguous(m4.F32, [256, 1, 1, 1], 4), contiguous(m4.F16, [320, N, 1, 1], 2),
+            contiguous(m4.I64, [1, 1, 1, 1], 8), contiguous(m4.I32, [1, 1, 1, 1], 4)]
+
+
+def test_supports_op_accepts_the_mistral_contract():
+    assert m4.supports_op(m4.OP_WKB, [Q8_WUK, QNOPE_M], QABS_M)
+    assert m4.supports_op(m4.OP_KQKV, [KC_M, QCUR_M, MASK_M], ATTN_M)
+    assert m4.supports_op(m4.OP_PHASE, [Q8_WUV, ATTN_M], OUT, [1] + [0] * 15)
+    assert m4.supports_op(m4.OP_PHASE, [Q8_WUV, PARTS_M], OUT, [2] + [0] * 15)
+    assert m4.supports_op(m4.OP_PHASE, [m4.Tensor(), PARTS_M], contiguous(m4.F32, [260, 32, 1, 1], 4),
+                          [3] + [0] * 15)
+    assert m4.supports_op(m4.OP_PHASE, _kvwrite_srcs(), KCUR, KVW_PARAMS)
+    assert not m4.supports_op(m4.OP_PHASE, [Q8_WUV, PARTS], OUT, [2] + [0] * 15)   # 516 records
 
 
 def _call(fn, args):
@@ -117,8 +159,11 @@ def test_entry_points_refuse_bad_operands_before_any_cuda_call():
     p.src[0], p.src[1], p.dst = WUV, ATTN, OUT
     p.op_params[0] = 7
     assert _call(lib.m4b_phase, p) == m4.EINVAL
-    p.op_params[0] = 0
-    assert _call(lib.m4b_phase, p) == m4.ENOTSUP
+    p.op_params[0] = 0                       # KV-write with W_UV / attn operands: malformed
+    assert _call(lib.m4b_phase, p) == m4.EINVAL
+    kv = m4.PhaseArgs()                      # a KV-write over a BASELINE-row cache: no such op
+    kv.src[3] = KC
+    assert _call(lib.m4b_phase, kv) == m4.ENOTSUP
     assert lib.m4b_kqkv(None, None) == m4.EINVAL
 
 
