@@ -44,6 +44,7 @@ SCALE = 1.0 / math.sqrt(DQ)
 PART = R + 4
 METRIC = "MLA decode attn layer-steps/s (262144 keys, 36 layers)"
 METRIC5 = "MLA decode attn layer-steps/s (16 ragged sequences, 36 layers)"
+METRIC_M = "MLA decode attn layer-steps/s (262144 keys, 36 layers, Mistral-Small-4 geometry)"
 UNIT = "layer-steps/s"
 
 
@@ -301,6 +302,90 @@ def slab_workload(args, rank, world, dev):
     return w
 
 
+def _q8_bytes(rows: int, K: int, g, dev):
+    """Q8_0 weights drawn on the device: int8 quants uniform on [-127, 127], f16 block scales
+    around 4e-4 (the size N(0, 0.02) weights quantize to); ggml's 34-byte block layout."""
+    import torch
+    nb = K // 32
+    quants = torch.randint(-127, 128, (rows, nb, 32), device=dev, generator=g, dtype=torch.int32)
+    scales = (4e-4 * (0.5 + torch.rand(rows, nb, 1, device=dev, generator=g))).half()
+    out = torch.empty(rows, nb, 34, dtype=torch.uint8, device=dev)
+    out[:, :, :2] = scales.view(torch.uint8)
+    out[:, :, 2:] = quants.to(torch.int8).view(torch.uint8)
+    return out.view(rows, nb * 34)
+
+
+def mistral_workload(args, rank, world, dev):
+    """Config 4 at the reference's own geometry (Mistral-Small-4: latent 256, KV row 320, Q8_0
+    weights), one GPU: per layer the engine's fused sequence -- KV-write of the new token's row
+    (PHASE 0), WKB, KQKV split-K partials, merge + W_UV (PHASE 2)."""
+    import torch
+    from aubier_b200 import m4
+    assert world == 1, "the Mistral-geometry line is a single-GPU measurement"
+    L, N = args.layers, args.keys
+    RM, DM, NOPEM, DQM = 256, 320, 64, 128
+    S = m4.default_splits(N)
+    g = torch.Generator(device=dev)
+    wuk, wuv, wkv, nw, kc, cur, qcur = [], [], [], [], [], [], []
+    q = torch.empty(L, H, DQM, device=dev)
+    for layer in range(L):
+        g.manual_seed(2000 * layer + 7)
+        wuk.append(_q8_bytes(H * RM, NOPEM, g, dev).view(H, RM, -1))
+        wuv.append(_q8_bytes(H * V, RM, g, dev).view(H, V, -1))
+        wkv.append(_q8_bytes(DM, 4096, g, dev))
+        nw.append(1.0 + 0.1 * torch.randn(RM, device=dev, generator=g))
+        kc.append(torch.randn(N, DM, device=dev, generator=g).half())
+        cur.append(torch.randn(4096, device=dev, generator=g))
+        q[layer] = torch.randn(H, DQM, device=dev, generator=g)
+        qc = torch.empty(H, DM, device=dev)
+        qc[:, RM:] = q[layer][:, NOPEM:]
+        qcur.append(qc)
+    kidx = torch.tensor([N - 1], dtype=torch.int64, device=dev)   # the new token's row
+    pos = torch.tensor([N - 1], dtype=torch.int32, device=dev)
+    kcur = torch.empty(DM, device=dev)
+    part = torch.empty(S, H, RM + 4, device=dev)
+    attn = torch.empty(H, RM, device=dev)
+    scale = 1.0 / math.sqrt(DQM)
+    w = Workload()
+    w.q, w.out = q, torch.empty(L, H, V, device=dev)
+    flags = m4.FLAG_PDL   # no KV_STATIC: the KV-write two launches earlier writes the cache
+
+    def step(e2e: bool = False):
+        for layer in range(L):
+            if e2e:
+                qcur[layer][:, RM:].copy_(q[layer][:, NOPEM:])
+            m4.phase_kvwrite(cur[layer], wkv[layer], nw[layer], kc[layer], kidx, pos, out=kcur,
+                             flags=flags)
+            m4.wkb(wuk[layer], q[layer][:, :NOPEM], out=qcur[layer][:, :RM], flags=flags)
+            m4.kqkv_partials(kc[layer], qcur[layer], None, scale, out=part, flags=flags)
+            m4.phase_combine_wvb(wuv[layer], part, out=w.out[layer], attn_out=attn, flags=flags)
+
+    def kq():
+        for layer in range(L):
+            m4.kqkv_partials(kc[layer], qcur[layer], None, scale, out=part,
+                             flags=m4.FLAG_PDL | m4.FLAG_KV_STATIC)
+
+    w.step, w.kq = step, kq
+    w.kq_kernel = "kqkv_partial_kernel<Geo<256>>"
+    w.kq_bytes = 640 * N + H * DM * 4
+    w.job_layer_bytes = (640 * N + H * RM * 68 + H * V * 272 + DM * 4352 + 4096 * 4 + H * DQM * 4
+                         + H * V * 4)
+    w.launches_per_step = 6 * L   # KV-write (2), WKB, partials, merge + W_UV (2)
+    w.traffic = None
+    w.metric = METRIC_M
+    w.config = {"workload": "BASELINE config 4 at the Mistral-Small-4 geometry of the reference "
+                            "(engine/m1_layer.h:47-55): 1 decode token, 262144-key f16 KV cache of "
+                            "320-wide rows, 36 layers, 32 heads, nope 64 / rope 64 / latent 256 / "
+                            "V 128, Q8_0 W_UK / W_UV / W_kva",
+                "keys": N, "layers": L, "keys_per_gpu": N, "splits_per_gpu": S,
+                "parallelism": "kv-slab x1",
+                "l2": f"inputs larger than L2 ({L} layers x {640 * N / 1e6:.0f} MB KV per step)",
+                "step": "KV-write -> WKB -> KQKV split-K partials -> PHASE combine+W_UV per layer, "
+                        "one CUDA graph per step"}
+    w.lengths = None
+    return w
+
+
 def ragged_workload(args, rank, world, dev):
     """Config 5: 16 sequences, one new token each, lengths uniform on [512, 65536] by seed, each
     layer's cache packed with per-sequence base/length; whole sequences per rank (LPT on keys),
@@ -379,7 +464,10 @@ def run_ours(args, rank: int, world: int) -> None:
 
     dev = torch.device("cuda", torch.cuda.current_device())
     L = args.layers
-    w = (ragged_workload if args.config == 5 else slab_workload)(args, rank, world, dev)
+    if args.geometry == "mistral":
+        w = mistral_workload(args, rank, world, dev)
+    else:
+        w = (ragged_workload if args.config == 5 else slab_workload)(args, rank, world, dev)
 
     def barrier():
         if world > 1:
@@ -474,7 +562,7 @@ def run_ours(args, rank: int, world: int) -> None:
         return
     cpu_baseline = None
     _restore_stdout()
-    if world == 1 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline and w.lengths is not None:
         try:
             cb = cpu_reference(w.lengths, reps=args.cpu_reps)
             cpu_baseline = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
@@ -536,6 +624,8 @@ def main():
                     help="config 4, N>1: fused NVLink exchange in the merge kernels, or NCCL")
     ap.add_argument("--config", type=int, choices=[4, 5], default=4,
                     help="4: 262,144-key slabs (the headline); 5: 16 ragged sequences")
+    ap.add_argument("--geometry", choices=["baseline", "mistral"], default="baseline",
+                    help="mistral: config 4 at the reference's own model geometry (1 GPU)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
