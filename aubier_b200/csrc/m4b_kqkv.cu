@@ -605,23 +605,17 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
             if (lane == 0) mbar_arrive(&C.red_full[grp]);
             ok = warp_wait(&C.red_full[grp], i & 1, abort_flag);
             if (!ok) break;
+            // lane j < 16 combines head j's four quadrant maxima (4 shared loads), then every
+            // lane gets all 16 by shuffles: fewer shared-memory accesses on the critical path,
+            // where they queue behind the tensor core's operand reads
+            float hm = -INFINITY;
+            if (lane < 16) {
+                const float* r = &C.red[i & 1][grp][0][lane];
+                hm = fmaxf(fmaxf(r[0], r[16]), fmaxf(r[32], r[48]));
+            }
             float tmax[16];
 #pragma unroll
-            for (int j4 = 0; j4 < 4; ++j4) {
-                float4 a = *reinterpret_cast<const float4*>(&C.red[i & 1][grp][0][4 * j4]);
-#pragma unroll
-                for (int qd = 1; qd < 4; ++qd) {
-                    const float4 b = *reinterpret_cast<const float4*>(&C.red[i & 1][grp][qd][4 * j4]);
-                    a.x = fmaxf(a.x, b.x);
-                    a.y = fmaxf(a.y, b.y);
-                    a.z = fmaxf(a.z, b.z);
-                    a.w = fmaxf(a.w, b.w);
-                }
-                tmax[4 * j4 + 0] = a.x;
-                tmax[4 * j4 + 1] = a.y;
-                tmax[4 * j4 + 2] = a.z;
-                tmax[4 * j4 + 3] = a.w;
-            }
+            for (int j = 0; j < 16; ++j) tmax[j] = __shfl_sync(0xffffffffu, hm, j);
             // Lazy rescale: keep the running max unless a head's max grows by > 2^8.
             bool need = false;
             float alpha[16];
