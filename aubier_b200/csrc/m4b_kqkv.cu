@@ -96,7 +96,9 @@ using GeoMistral = Geo<256>;
 constexpr int NTHREADS = 320;
 constexpr int TM_S = 0;
 constexpr int TM_O = 64;
-constexpr float RESCALE_THRESH = 8.0f;  // log2 units: P stays <= 2^8 between rescales
+// log2 units: P = 2^(s - m) stays <= 2^15 (exact in f16, below its 65504 limit) while the running
+// max m is stale; a head is rescaled only when a score would exceed that
+constexpr float GROW_THRESH = 15.0f;
 constexpr float LOG2E = 1.4426950408889634f;
 
 // One run of consecutive tiles of one window, as this CTA processes it.
@@ -116,7 +118,8 @@ struct Ctrl {
     uint64_t empty[NSLOT];
     uint64_t s_full[2], p_full[2];
     uint64_t q_full, o_done, o_full;
-    uint64_t red_full[2];   // per head group: the 4 warps' tile maxima are in red[]
+    uint64_t red_full[2];   // per head group, once per tile: the 4 warps' flags / maxima are in
+    uint64_t red2_full[2];  // per head group, rare: the exact maxima after a raised flag
     uint64_t redl_full[2];  // per head group: the 4 warps' row sums are in red_l[]
     uint32_t tmem_base;
     int abort_flag;
@@ -124,10 +127,19 @@ struct Ctrl {
     int ntot;     // tiles of this CTA (sum over its segments)
     alignas(16) float red[2][2][4][16];  // [tile parity][group][quadrant][head], read as float4
     alignas(16) float red_l[2][4][16];   // [group][quadrant][head]
+    alignas(16) int flag[2][2][4];       // [tile parity][group][quadrant]: a score outgrew the max
 };
 static_assert(sizeof(Ctrl) <= CTRL_BYTES, "control block too large");
 static_assert(offsetof(Ctrl, red) % 16 == 0 && offsetof(Ctrl, red_l) % 16 == 0,
               "reduction buffers are read with 16-byte vector loads");
+
+// 2^x by the special-function unit (ex2.approx: relative error ~2^-22, far below the f16 rounding
+// that P gets next; 2^-inf = +0)
+__device__ __forceinline__ float ex2_fast(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
@@ -261,6 +273,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
             mbar_init(&C.s_full[b], 1);
             mbar_init(&C.p_full[b], 8);
             mbar_init(&C.red_full[b], 4);
+            mbar_init(&C.red2_full[b], 4);
             mbar_init(&C.redl_full[b], 4);
         }
         mbar_init(&C.q_full, 256);
@@ -534,6 +547,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
         }
         bool ok = true;
         int nflush = 0;
+        int nrare = 0;   // red2_full phases used (uniform in the group)
         // ---- a segment's partial record (o[512], m, l) per head; o is read from TMEM once the
         // segment's last MMA2 is complete (bar, parity)
         auto flush = [&](const Seg& sg, uint64_t* bar, uint32_t parity) {
@@ -599,36 +613,60 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
                 t = t + mv;
                 s[j] = valid ? t * LOG2E : -INFINITY;
             }
-            const float wmax = transpose_reduce16<true>(s, lane);
-            if ((lane & 1) == 0) C.red[i & 1][grp][quad][lane >> 1] = wmax;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&C.red_full[grp]);
-            ok = warp_wait(&C.red_full[grp], i & 1, abort_flag);
-            if (!ok) break;
-            // lane j < 16 combines head j's four quadrant maxima (4 shared loads), then every
-            // lane gets all 16 by shuffles: fewer shared-memory accesses on the critical path,
-            // where they queue behind the tensor core's operand reads
-            float hm = -INFINITY;
-            if (lane < 16) {
-                const float* r = &C.red[i & 1][grp][0][lane];
-                hm = fmaxf(fmaxf(r[0], r[16]), fmaxf(r[32], r[48]));
-            }
-            float tmax[16];
+            // The running max m_run is shared by the group's 4 warps (their keys feed one O per
+            // head).  It only has to bound the scores, not track them: P = 2^(s - m_run) is exact
+            // in f16 up to 2^15.  So a tile normally costs one vote per warp ("does any score exceed
+            // m_run + 15?"); the exact maxima are exchanged, and m_run raised, only on a head's
+            // first keys or when a vote is raised (rare) -- shared-memory and shuffle traffic queue
+            // behind the tensor core's operand reads, and this keeps it off the critical path.
+            bool fresh = false;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) tmax[j] = __shfl_sync(0xffffffffu, hm, j);
-            // Lazy rescale: keep the running max unless a head's max grows by > 2^8.
+            for (int j = 0; j < 16; ++j) fresh |= (m_run[j] == -INFINITY);   // uniform in the group
+            bool exchange = fresh;
+            if (!fresh) {
+                bool big = false;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) big |= (s[j] - m_run[j] > GROW_THRESH);
+                const bool wbig = __any_sync(0xffffffffu, big);
+                if (lane == 0) C.flag[i & 1][grp][quad] = wbig ? 1 : 0;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&C.red_full[grp]);
+                ok = warp_wait(&C.red_full[grp], i & 1, abort_flag);
+                if (!ok) break;
+                const int4 f = *reinterpret_cast<const int4*>(&C.flag[i & 1][grp][0]);
+                exchange = (f.x | f.y | f.z | f.w) != 0;
+            }
             bool need = false;
             float alpha[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                alpha[j] = 1.0f;
-                const float mn = fmaxf(m_run[j], tmax[j]);
-                if (m_run[j] == -INFINITY) {
-                    m_run[j] = mn;          // nothing accumulated yet for this head
-                } else if (mn - m_run[j] > RESCALE_THRESH) {
-                    alpha[j] = exp2f(m_run[j] - mn);
-                    m_run[j] = mn;
-                    need = true;
+            for (int j = 0; j < 16; ++j) alpha[j] = 1.0f;
+            if (exchange) {
+                const float wmax = transpose_reduce16<true>(s, lane);
+                if ((lane & 1) == 0) C.red[i & 1][grp][quad][lane >> 1] = wmax;
+                __syncwarp();
+                uint64_t* bar = fresh ? &C.red_full[grp] : &C.red2_full[grp];
+                const uint32_t par = fresh ? (i & 1) : (nrare & 1);
+                if (lane == 0) mbar_arrive(bar);
+                ok = warp_wait(bar, par, abort_flag);
+                if (!ok) break;
+                if (!fresh) ++nrare;
+                // lane j < 16 combines head j's four quadrant maxima, then all lanes get all 16
+                float hm = -INFINITY;
+                if (lane < 16) {
+                    const float* r = &C.red[i & 1][grp][0][lane];
+                    hm = fmaxf(fmaxf(r[0], r[16]), fmaxf(r[32], r[48]));
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const float tmax = __shfl_sync(0xffffffffu, hm, j);
+                    const float mn = fmaxf(m_run[j], tmax);
+                    if (m_run[j] == -INFINITY) {
+                        m_run[j] = mn;          // nothing accumulated yet for this head
+                    } else if (mn > m_run[j]) {
+                        alpha[j] = exp2f(m_run[j] - mn);
+                        m_run[j] = mn;
+                        need = true;
+                    }
                 }
             }
             if (need) {   // uniform across the group: every thread computed the same maxima
@@ -653,7 +691,9 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
             uint8_t* const prow = prow0 + (i & 1) * P_BYTES;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-                const float pv = (s[j] == -INFINITY) ? 0.0f : exp2f(s[j] - m_run[j]);
+                // masked key: 2^-inf = 0; a head with no valid key yet has m_run = -inf and the
+                // difference NaN, which fmaxf also turns into -inf
+                const float pv = ex2_fast(fmaxf(s[j] - m_run[j], -INFINITY));
                 l_part[j] += pv;
                 const int h = 16 * grp + j;
                 *reinterpret_cast<__half*>(prow + h * 128 + ((punit ^ (h & 7)) << 4)) =
