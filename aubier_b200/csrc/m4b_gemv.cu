@@ -144,6 +144,156 @@ wvb_f16_kernel(const __half* __restrict__ w, const float* __restrict__ x, Rows x
     }
 }
 
+// ---- Token batches (nt > 1, the ragged decode path).  The loops above would read each token's
+// activation from L2 inside the token loop -- one dependent L2 round trip per token -- and reduce
+// every (row, token) dot with its own shuffle tree.  Here a CTA (one head: 64 WKB rows or 16 WVB
+// rows) first stages all nt activations of its head in shared memory, rounded to f16 (one L2 round
+// trip), and a chunk of tokens is reduced at once: each lane holds rows x tokens partial dots and
+// one xor butterfly leaves every lane with one finished (row, token) sum.  The per-lane dot and the
+// butterfly's pairing are those of the single-token kernels, so results are bit-identical to them.
+
+// Sum each of N values over the N lanes of an xor group (lanes differing in their low log2(N)
+// bits); afterwards lane L holds the sum of value index (L & (N - 1)).
+template <int N>
+__device__ __forceinline__ float xor_transpose_reduce(float (&v)[N], int lane) {
+#pragma unroll
+    for (int n = N, off = N / 2; n > 1; n >>= 1, off >>= 1) {
+        const bool upper = (lane & off) != 0;
+        const int half = n >> 1;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float send = upper ? v[i] : v[i + half];
+            const float keep = upper ? v[i + half] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+    }
+    return v[0];
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Stage n_units units of 8 activations (f32 -> f16, round to nearest even) of one head:
+// unit i = token i / upt, columns 8 * (i % upt) .. +7; tokens >= nt are zero.
+__device__ __forceinline__ void stage_tokens(__half* xs, const float* __restrict__ x, Rows xr, int h,
+                                             int nt, int ntp, int upt, int nthreads) {
+    for (int i = threadIdx.x; i < ntp * upt; i += nthreads) {
+        const int t = i / upt, u = i % upt;
+        uint4 pk = make_uint4(0u, 0u, 0u, 0u);
+        if (t < nt) {
+            const float* src = x + static_cast<size_t>(t) * xr.ts + static_cast<size_t>(h) * xr.hs + 8 * u;
+            float f[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[j] = src[j];
+            pk.x = pack_h2(f[0], f[1]);
+            pk.y = pack_h2(f[2], f[3]);
+            pk.z = pack_h2(f[4], f[5]);
+            pk.w = pack_h2(f[6], f[7]);
+        }
+        reinterpret_cast<uint4*>(xs)[i] = pk;
+    }
+}
+
+constexpr int WKB_TCH = 4;    // tokens per butterfly: 4 row pairs x 4 tokens = 16 values, 16 lanes
+constexpr int WVB_TCH = 16;   // 2 rows x 16 tokens = 32 values, 32 lanes
+
+__global__ void __launch_bounds__(WKB_THREADS)
+wkb_f16_batch_kernel(const __half* __restrict__ w, const float* __restrict__ q, Rows qr,
+                     float* __restrict__ out, Rows outr, int nt) {
+    extern __shared__ __align__(16) uint8_t dyn_smem[];
+    __half* xs = reinterpret_cast<__half*>(dyn_smem);   // [ntp][kNope]
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int row0 = (blockIdx.x * (WKB_THREADS / 32) + warp) * WKB_ROWS_PER_WARP;
+    const int h = (blockIdx.x * (WKB_THREADS / 32) * WKB_ROWS_PER_WARP) / kLatent;   // one head per CTA
+    const int r0 = row0 % kLatent;
+    const int hw = lane >> 4;
+    const int l16 = lane & 15;
+    const int ntp = (nt + WKB_TCH - 1) / WKB_TCH * WKB_TCH;
+
+    uint4 wv[WKB_ROWS_PER_WARP / 2];
+#pragma unroll
+    for (int it = 0; it < WKB_ROWS_PER_WARP / 2; ++it)
+        wv[it] = ldg_stream(w + static_cast<size_t>(row0 + 2 * it + hw) * kNope + 8 * l16);
+    pdl_launch_dependents();
+    pdl_wait();
+    stage_tokens(xs, q, qr, h, nt, ntp, kNope / 8, WKB_THREADS);
+    float wf[WKB_ROWS_PER_WARP / 2][8];
+#pragma unroll
+    for (int it = 0; it < WKB_ROWS_PER_WARP / 2; ++it) unpack8(wv[it], wf[it]);
+    __syncthreads();
+    for (int c = 0; c < ntp; c += WKB_TCH) {
+        float v[16];
+#pragma unroll
+        for (int tt = 0; tt < WKB_TCH; ++tt) {
+            float xf[8];
+            unpack8(*reinterpret_cast<const uint4*>(xs + (c + tt) * kNope + 8 * l16), xf);
+#pragma unroll
+            for (int it = 0; it < WKB_ROWS_PER_WARP / 2; ++it) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc = fmaf(wf[it][j], xf[j], acc);
+                v[WKB_TCH * it + tt] = acc;
+            }
+        }
+        const float r = xor_transpose_reduce<16>(v, lane);
+        const int it = l16 / WKB_TCH, t = c + l16 % WKB_TCH;
+        if (t < nt) out[static_cast<size_t>(t) * outr.ts + h * outr.hs + r0 + 2 * it + hw] = r;
+    }
+}
+
+__global__ void __launch_bounds__(WVB_THREADS)
+wvb_f16_batch_kernel(const __half* __restrict__ w, const float* __restrict__ x, Rows xr,
+                     float* __restrict__ out, Rows outr, int nt) {
+    extern __shared__ __align__(16) uint8_t dyn_smem[];
+    __half* xs = reinterpret_cast<__half*>(dyn_smem);   // [ntp][kLatent]
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int row0 = (blockIdx.x * (WVB_THREADS / 32) + warp) * WVB_ROWS_PER_WARP;
+    const int h = (blockIdx.x * (WVB_THREADS / 32) * WVB_ROWS_PER_WARP) / kVHead;   // one head per CTA
+    const int j0 = row0 % kVHead;
+    const int ntp = (nt + WVB_TCH - 1) / WVB_TCH * WVB_TCH;
+
+    uint4 wv[WVB_ROWS_PER_WARP][2];
+#pragma unroll
+    for (int it = 0; it < WVB_ROWS_PER_WARP; ++it)
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+            wv[it][u] = ldg_stream(w + static_cast<size_t>(row0 + it) * kLatent + 256 * u + 8 * lane);
+    pdl_wait();
+    stage_tokens(xs, x, xr, h, nt, ntp, kLatent / 8, WVB_THREADS);
+    float wf[WVB_ROWS_PER_WARP][2][8];
+#pragma unroll
+    for (int it = 0; it < WVB_ROWS_PER_WARP; ++it)
+#pragma unroll
+        for (int u = 0; u < 2; ++u) unpack8(wv[it][u], wf[it][u]);
+    __syncthreads();
+    for (int c = 0; c < ntp; c += WVB_TCH) {
+        float v[32];
+#pragma unroll
+        for (int tt = 0; tt < WVB_TCH; ++tt) {
+            float xf[2][8];
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+                unpack8(*reinterpret_cast<const uint4*>(xs + (c + tt) * kLatent + 256 * u + 8 * lane), xf[u]);
+#pragma unroll
+            for (int it = 0; it < WVB_ROWS_PER_WARP; ++it) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int u = 0; u < 2; ++u)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc = fmaf(wf[it][u][j], xf[u][j], acc);
+                v[WVB_TCH * it + tt] = acc;
+            }
+        }
+        const float r = xor_transpose_reduce<32>(v, lane);
+        const int it = lane / WVB_TCH, t = c + lane % WVB_TCH;
+        if (t < nt) out[static_cast<size_t>(t) * outr.ts + h * outr.hs + j0 + it] = r;
+    }
+}
+
 }  // namespace gemv
 
 cudaError_t launch_wkb_f16(const void* w, const float* q, Rows qr, float* out, Rows outr, int nt,
@@ -151,6 +301,13 @@ cudaError_t launch_wkb_f16(const void* w, const float* q, Rows qr, float* out, R
     using namespace gemv;
     constexpr int rows = kHeads * kLatent;
     constexpr int grid = rows / (WKB_ROWS_PER_WARP * (WKB_THREADS / 32));
+    static_assert(kLatent % (WKB_ROWS_PER_WARP * (WKB_THREADS / 32)) == 0, "a CTA spans one head");
+    if (nt > 1) {
+        const int ntp = (nt + WKB_TCH - 1) / WKB_TCH * WKB_TCH;
+        return launch(wkb_f16_batch_kernel, dim3(grid), dim3(WKB_THREADS),
+                      static_cast<size_t>(ntp) * kNope * sizeof(__half), stream, flags,
+                      static_cast<const __half*>(w), q, qr, out, outr, nt);
+    }
     return launch(wkb_f16_kernel, dim3(grid), dim3(WKB_THREADS), 0, stream, flags,
                   static_cast<const __half*>(w), q, qr, out, outr, nt);
 }
@@ -160,6 +317,17 @@ cudaError_t launch_wvb_f16(const void* w, const float* x, Rows xr, float* out, R
     using namespace gemv;
     constexpr int rows = kHeads * kVHead;
     constexpr int grid = rows / (WVB_ROWS_PER_WARP * (WVB_THREADS / 32));
+    static_assert(kVHead % (WVB_ROWS_PER_WARP * (WVB_THREADS / 32)) == 0, "a CTA spans one head");
+    if (nt > 1) {
+        const int ntp = (nt + WVB_TCH - 1) / WVB_TCH * WVB_TCH;
+        const size_t smem = static_cast<size_t>(ntp) * kLatent * sizeof(__half);   // <= 64 KB
+        const cudaError_t e = note(cudaFuncSetAttribute(
+            wvb_f16_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            static_cast<int>(kMaxSeqs * kLatent * sizeof(__half))));
+        if (e != cudaSuccess) return e;
+        return launch(wvb_f16_batch_kernel, dim3(grid), dim3(WVB_THREADS), smem, stream, flags,
+                      static_cast<const __half*>(w), x, xr, out, outr, nt);
+    }
     return launch(wvb_f16_kernel, dim3(grid), dim3(WVB_THREADS), 0, stream, flags,
                   static_cast<const __half*>(w), x, xr, out, outr, nt);
 }

@@ -85,6 +85,24 @@ def test_wvb_token_batch_matches_oracle(m4):
         assert rel_to_max(got[t], O.wvb(w_uv, x[t])) <= ATTN_TOL
 
 
+@pytest.mark.parametrize("nt", [2, 4, 16, 17, 64])
+def test_token_batch_equals_single_token_calls(m4, nt):
+    """The batched gemvs stage the tokens in shared memory and reduce several (row, token) dots
+    per butterfly; the per-lane dot and the pairing of the reduction are the single-token
+    kernels', so every token's result is bit-identical to a one-token call."""
+    _, w_uk, _, w_uv = make_layer(68, 1)
+    qd = dev(tokens(69, nt))
+    wk = dev(w_uk)
+    batch = host(m4.wkb(wk, qd[:, :, :G.nope]))
+    for t in range(nt):
+        assert np.array_equal(batch[t], host(m4.wkb(wk, qd[t, :, :G.nope])))
+    xd = dev(normal(70, nt * G.H * G.R).astype(np.float32).reshape(nt, G.H, G.R))
+    wv = dev(w_uv)
+    b2 = host(m4.phase_wvb(wv, xd))
+    for t in range(nt):
+        assert np.array_equal(b2[t], host(m4.phase_wvb(wv, xd[t])))
+
+
 def test_token_batch_limits(m4):
     _, w_uk, _, w_uv = make_layer(67, 1)
     with pytest.raises(m4.M4Error):
