@@ -561,7 +561,14 @@ int m4b_phase(const m4b_phase_args* a, m4b_stream_t stream) {
         return status_of(wvb(static_cast<const float*>(a->src[1].data), xr, outr,
                              static_cast<int>(a->src[1].ne[1]), a->flags));
     }
-    // phase 2: merge the partial records, then W_UV (one node, two launches)
+    // phase 2: merge the partial records, then W_UV -- one launch at the f16 geometry (attn is
+    // written only when the caller passed src[2]), two at the Q8_0 geometry
+    const int n_rec = static_cast<int>(a->src[1].ne[2]);
+    if (geom != kGeomMistral && 2 * static_cast<size_t>(n_rec) * sizeof(float) <= 48 * 1024)
+        return status_of(launch_kqkv_combine_wvb(
+            static_cast<const float*>(a->src[1].data), n_rec, a->src[0].data,
+            a->src[2].data != nullptr ? attn : nullptr, attn_hs, out, out_hs,
+            a->flags & M4B_FLAG_PDL, s));
     cudaError_t e = launch_kqkv_combine(static_cast<const float*>(a->src[1].data),
                                         static_cast<int>(a->src[1].ne[2]), kGeo[geom].latent, attn,
                                         attn_hs, a->flags & M4B_FLAG_PDL, s);

@@ -56,6 +56,10 @@ cudaError_t launch_kqkv_combine(const float* part, int S, int latent, float* out
 
 // Ragged batch: merge each token's records (written by launch_kqkv_partials with seq_base set)
 // into out[t * out_ts + h * out_hs + d].
+// PHASE selector 2 (f16 W_UV): merge + W_UV in one launch; attn_out may be null.
+cudaError_t launch_kqkv_combine_wvb(const float* part, int S, const void* w_uv, float* attn_out,
+                                    int64_t attn_hs, float* out, int64_t out_hs, uint32_t flags,
+                                    cudaStream_t stream);
 cudaError_t launch_kqkv_ragged_combine(const float* part, const int32_t* seq_base,
                                        const int32_t* seq_len, int n_seq, int64_t n_rows,
                                        int splits, int latent, float* out, int64_t out_hs,

@@ -39,6 +39,7 @@
 // both products accumulate in f32.
 #include <cstddef>
 #include <type_traits>
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
@@ -817,6 +818,178 @@ kqkv_combine_kernel(const float* __restrict__ part, int S, float* __restrict__ o
                   out + h * out_hs, record_out, s_alpha);
 }
 
+// PHASE selector 2 in one launch: the LSE merge of one head's 128-column block (merge_head's
+// arithmetic and order, so attn is bit-identical to kqkv_combine_kernel's) followed by that block's
+// share of W_UV: out[h][j] = sum over the R / 128 column blocks of sum_r W_UV[h][j][r] * f16(attn[h][r]).
+// The blocks of a head form a thread-block cluster; rank 0 adds the blocks' partial rows in rank order
+// through distributed shared memory (plain loads, no multicast), so the result is deterministic.  All
+// record loads of a warp (m, l, and up to RB records' 128 columns) are issued before the first use:
+// one L2 round trip where the two-launch form waited on several.  The block's W_UV slice (32 KB) is
+// loaded before griddepcontrol.wait, overlapping the KQKV tail.  Compared with the two launches it
+// replaces, only the order of W_UV's additions differs (per block, then across blocks).
+constexpr int CWV_RB = 19;   // records per warp in flight: 8 warps x 19 >= 148 splits
+
+__device__ __forceinline__ uint4 ldg_nc_u4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+template <int N>
+__device__ __forceinline__ float butterfly_transpose_sum(float (&v)[N], int lane) {
+#pragma unroll
+    for (int n = N, off = N / 2; n > 1; n >>= 1, off >>= 1) {
+        const bool upper = (lane & off) != 0;
+        const int half = n >> 1;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float send = upper ? v[i] : v[i + half];
+            const float keep = upper ? v[i + half] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+    }
+    return v[0];   // lane L: the sum over its xor group of value index (L & (N - 1))
+}
+
+template <int R>
+__global__ void __cluster_dims__(1, R / 128, 1) __launch_bounds__(CMB_THREADS)
+kqkv_combine_wvb_kernel(const float* __restrict__ part, int S, const __half* __restrict__ w_uv,
+                        float* __restrict__ attn_out, int64_t attn_hs, float* __restrict__ out,
+                        int64_t out_hs) {
+    namespace cg = cooperative_groups;
+    extern __shared__ float s_ml[];   // [2][S]: m then alpha, l
+    __shared__ __align__(16) float s_red[CMB_THREADS / 32][128];
+    __shared__ float s_m[CMB_THREADS / 32], s_l[CMB_THREADS / 32];
+    __shared__ __align__(16) __half s_x[128];
+    __shared__ float s_part[kVHead];
+    const int h = blockIdx.x;
+    const int d0 = blockIdx.y * 128;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t ss = static_cast<size_t>(kHeads) * (R + 4);
+    const float* ph = part + static_cast<size_t>(h) * (R + 4);
+
+    // W_UV[h][j][d0 .. d0+127]: warp w holds rows 16w .. 16w+15, a half-warp one row per step
+    const int hw = lane >> 4, l16 = lane & 15;
+    uint4 wv[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int j = 16 * warp + 2 * k + hw;
+        wv[k] = ldg_nc_u4(w_uv + (static_cast<size_t>(h) * kVHead + j) * R + d0 + 8 * l16);
+    }
+    pdl_wait();
+
+    float4 ov[CWV_RB];
+    auto load_records = [&](int sb) {
+#pragma unroll
+        for (int k = 0; k < CWV_RB; ++k) {
+            const int s = sb + warp + 8 * k;
+            ov[k] = s < S ? __ldg(reinterpret_cast<const float4*>(ph + s * ss + d0 + 4 * lane))
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    load_records(0);
+    float* s_ms = s_ml;
+    float* s_ls = s_ml + S;
+    float m = -INFINITY;
+    for (int s = tid; s < S; s += CMB_THREADS) {
+        const float ms = __ldg(ph + s * ss + R);
+        s_ms[s] = ms;
+        s_ls[s] = __ldg(ph + s * ss + (R + 1));
+        m = fmaxf(m, ms);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (lane == 0) s_m[warp] = m;
+    __syncthreads();
+    float mstar = s_m[0];
+#pragma unroll
+    for (int w = 1; w < CMB_THREADS / 32; ++w) mstar = fmaxf(mstar, s_m[w]);
+    float lsum = 0.0f;
+    for (int s = tid; s < S; s += CMB_THREADS) {
+        const float ms = s_ms[s];
+        const float a = (ms > -INFINITY) ? exp2f(ms - mstar) : 0.0f;
+        s_ms[s] = a;   // alpha
+        lsum += a * s_ls[s];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
+    if (lane == 0) s_l[warp] = lsum;
+    __syncthreads();
+
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sb = 0;;) {
+#pragma unroll
+        for (int k = 0; k < CWV_RB; ++k) {
+            const int s = sb + warp + 8 * k;
+            if (s < S) {
+                const float a = s_ms[s];
+                acc.x = fmaf(a, ov[k].x, acc.x);
+                acc.y = fmaf(a, ov[k].y, acc.y);
+                acc.z = fmaf(a, ov[k].z, acc.z);
+                acc.w = fmaf(a, ov[k].w, acc.w);
+            }
+        }
+        sb += 8 * CWV_RB;
+        if (sb >= S) break;
+        load_records(sb);
+    }
+    *reinterpret_cast<float4*>(&s_red[warp][4 * lane]) = acc;
+    __syncthreads();
+    if (tid < 128) {
+        float o = 0.0f, l = 0.0f;
+#pragma unroll
+        for (int w = 0; w < CMB_THREADS / 32; ++w) {
+            o += s_red[w][tid];
+            l += s_l[w];
+        }
+        const float at = (mstar > -INFINITY) ? o / l : 0.0f;
+        if (attn_out != nullptr) attn_out[h * attn_hs + d0 + tid] = at;
+        s_x[tid] = __float2half_rn(at);
+    }
+    __syncthreads();
+
+    // this block's share of W_UV: 8 rows per half-warp, a lane's 8 columns, one transpose-sum
+    float xf[8];
+    {
+        const uint4 xu = *reinterpret_cast<const uint4*>(s_x + 8 * l16);
+        const __half2* x2 = reinterpret_cast<const __half2*>(&xu);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(x2[i]);
+            xf[2 * i] = f.x;
+            xf[2 * i + 1] = f.y;
+        }
+    }
+    float dots[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const __half2* w2 = reinterpret_cast<const __half2*>(&wv[k]);
+        float a = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(w2[i]);
+            a = fmaf(f.x, xf[2 * i], a);
+            a = fmaf(f.y, xf[2 * i + 1], a);
+        }
+        dots[k] = a;
+    }
+    float r = butterfly_transpose_sum<8>(dots, lane);   // lanes 8 apart hold the two half-sums
+    r += __shfl_xor_sync(0xffffffffu, r, 8);
+    if ((l16 & 8) == 0) s_part[16 * warp + 2 * l16 + hw] = r;
+
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    if (cluster.block_rank() == 0 && tid < kVHead) {
+        float o = 0.0f;
+#pragma unroll
+        for (int b = 0; b < R / 128; ++b) o += cluster.map_shared_rank(s_part, b)[tid];
+        out[h * out_hs + tid] = o;
+    }
+    cluster.sync();   // the other blocks' shared memory stays alive until rank 0 has read it
+}
+
 // Ragged batch: grid (32 heads, R / 128 column blocks, n_seq tokens).  Token t's window covers tiles
 // [ps, ps + ts) of the concatenation; the CTAs owning them wrote their records for t at slots
 // c + t (kqkv_partial_kernel), so the records to merge are the contiguous slots
@@ -929,6 +1102,16 @@ cudaError_t launch_kqkv_combine(const float* part, int S, int latent, float* out
                       stream, flags, part, S, out, out_hs, 0);
     return launch(kq::kqkv_combine_kernel<kLatent>, dim3(kHeads, kLatent / 128),
                   dim3(kq::CMB_THREADS), smem, stream, flags, part, S, out, out_hs, 0);
+}
+
+cudaError_t launch_kqkv_combine_wvb(const float* part, int S, const void* w_uv, float* attn_out,
+                                    int64_t attn_hs, float* out, int64_t out_hs, uint32_t flags,
+                                    cudaStream_t stream) {
+    const size_t smem = 2 * static_cast<size_t>(S) * sizeof(float);
+    if (smem > 48 * 1024) return note(cudaErrorInvalidValue);
+    return launch(kq::kqkv_combine_wvb_kernel<kLatent>, dim3(kHeads, kLatent / 128),
+                  dim3(kq::CMB_THREADS), smem, stream, flags, part, S,
+                  static_cast<const __half*>(w_uv), attn_out, attn_hs, out, out_hs);
 }
 
 cudaError_t launch_kqkv_ragged_combine(const float* part, const int32_t* seq_base,

@@ -182,6 +182,22 @@ def test_combine_wvb_matches_oracle(m4):
     assert np.array_equal(out, out2)
 
 
+def test_combine_wvb_one_launch_equals_two_steps(m4):
+    """PHASE selector 2 merges and applies W_UV in one launch: its attn is bit-identical to the
+    single-window op's merge of the same records, and its output matches W_UV applied to that attn
+    (only the order of W_UV's additions differs)."""
+    N = 30000
+    q, w_uk, kc, w_uv = make_layer(43, N)
+    qcur, kcd = dev(qcur_of(q, w_uk)), dev(kc)
+    mask = dev(window_mask(N, 700, 25000))
+    part = m4.kqkv_partials(kcd, qcur, mask, SCALE)
+    attn = torch.empty(G.H, G.R, device="cuda")
+    wuv = dev(w_uv)
+    out = host(m4.phase_combine_wvb(wuv, part, attn_out=attn))
+    assert np.array_equal(host(attn), host(m4.kqkv(kcd, qcur, mask, SCALE)))
+    assert rel_to_max(out, host(m4.phase_wvb(wuv, attn))) <= 1e-5
+
+
 def test_merge_records_two_level_equals_direct(m4):
     """PHASE selector 3 (the multi-GPU exchange payload): merging groups of partial records into
     one record each, then merging those, equals merging all records at once."""
