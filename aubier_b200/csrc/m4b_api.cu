@@ -307,7 +307,7 @@ int check_phase(const m4b_phase_args& a, int* geom) {
         case 2: {
             int rc = check_wuv(a.src[0], geom);
             if (rc != M4B_OK) return rc;
-            rc = check_partials(a.src[1], 0, *geom);
+            rc = check_partials(a.src[1], kMaxRecords, *geom);
             if (rc != M4B_OK) return rc;
             if (a.src[2].data != nullptr && check_attn(a.src[2], *geom) != M4B_OK) return M4B_EINVAL;
             return check_phase_dst(a.dst);
@@ -315,7 +315,7 @@ int check_phase(const m4b_phase_args& a, int* geom) {
         case 3: {   // merge records -> one record per head (additive, for the GPU exchange)
             const int g = record_geometry(a.src[1]);
             if (g < 0) return M4B_EINVAL;
-            int rc = check_partials(a.src[1], 0, g);
+            int rc = check_partials(a.src[1], kMaxRecords, g);
             if (rc != M4B_OK) return rc;
             const m4b_tensor& d = a.dst;
             if (d.type != M4B_TYPE_F32 || d.ne[0] != kGeo[g].part || d.ne[1] != kHeads ||

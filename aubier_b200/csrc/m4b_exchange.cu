@@ -92,58 +92,21 @@ constexpr int THREADS = 256;
 __global__ void __launch_bounds__(THREADS)
 publish_kernel(const float* __restrict__ part, int S, PeerPtrs peers, char* local, int world,
                int rank, Layout L) {
-    extern __shared__ float s_alpha[];   // [S]
+    extern __shared__ float s_ml[];   // [2][S]
     __shared__ __align__(16) float s_red[THREADS / 32][128];   // written as float4
     __shared__ float s_m[THREADS / 32], s_l[THREADS / 32];
+    static_assert(THREADS == kq::CMB_THREADS, "the merge helper assumes the combine's block size");
     pdl_wait();
     const int h = blockIdx.x;
     const int d0 = blockIdx.y * 128;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tid = threadIdx.x;
     const size_t ss = static_cast<size_t>(kHeads) * kPartStride;
     const float* ph = part + static_cast<size_t>(h) * kPartStride;
     const uint64_t e = *reinterpret_cast<volatile uint64_t*>(local + L.epoch_off) + 1;
-
-    float m = -INFINITY;
-    for (int s = tid; s < S; s += THREADS) m = fmaxf(m, __ldg(ph + s * ss + kPartM));
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    if (lane == 0) s_m[warp] = m;
-    __syncthreads();
-    float mstar = s_m[0];
-#pragma unroll
-    for (int w = 1; w < THREADS / 32; ++w) mstar = fmaxf(mstar, s_m[w]);
-    float lsum = 0.0f;
-    for (int s = tid; s < S; s += THREADS) {
-        const float ms = __ldg(ph + s * ss + kPartM);
-        const float a = (ms > -INFINITY) ? exp2f(ms - mstar) : 0.0f;
-        s_alpha[s] = a;
-        lsum += a * __ldg(ph + s * ss + kPartL);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
-    if (lane == 0) s_l[warp] = lsum;
-    __syncthreads();
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    const float* col = ph + d0 + 4 * lane;
-#pragma unroll 4
-    for (int s = warp; s < S; s += THREADS / 32) {
-        const float a = s_alpha[s];
-        const float4 v = __ldg(reinterpret_cast<const float4*>(col + s * ss));
-        acc.x = fmaf(a, v.x, acc.x);
-        acc.y = fmaf(a, v.y, acc.y);
-        acc.z = fmaf(a, v.z, acc.z);
-        acc.w = fmaf(a, v.w, acc.w);
-    }
-    *reinterpret_cast<float4*>(&s_red[warp][4 * lane]) = acc;
-    __syncthreads();
+    float mstar, l, o;
+    kq::merge_block_inflight<kLatent>(ph, S, ss, d0, s_ml, s_red, s_m, s_l, mstar, l, o);
     const uint32_t e32 = static_cast<uint32_t>(e);
     if (tid < 128) {
-        float o = 0.0f, l = 0.0f;
-#pragma unroll
-        for (int w = 0; w < THREADS / 32; ++w) {
-            o += s_red[w][tid];
-            l += s_l[w];
-        }
 #pragma unroll
         for (int p = 0; p < kMaxWorld; ++p) {   // unrolled: the peer table stays in registers
             if (p >= world) break;
@@ -353,7 +316,7 @@ M4B_API int m4b_exchange_publish(m4b_exchange* x, const m4b_phase_args* a, m4b_s
     xch::PeerPtrs pp;
     for (int r = 0; r < kMaxWorld; ++r) pp.p[r] = r < x->world ? x->peer[r] : nullptr;
     const int S = static_cast<int>(a->src[1].ne[2]);
-    const size_t smem = static_cast<size_t>(S) * sizeof(float);
+    const size_t smem = 2 * static_cast<size_t>(S) * sizeof(float);
     if (smem > 48 * 1024) return M4B_EINVAL;
     return status_of(launch(xch::publish_kernel, dim3(kHeads, kLatent / 128), dim3(xch::THREADS),
                             smem, reinterpret_cast<cudaStream_t>(stream), a->flags,

@@ -27,6 +27,7 @@ constexpr int kPartL = kLatent + 1;
 
 constexpr int kTileKeys = 128;   // keys per KQKV tile (the tcgen05 MMA M dimension)
 constexpr int kMaxSplits = 148;  // one persistent CTA per B200 SM
+constexpr int kMaxRecords = 6144;  // partial records one merge accepts (m and l staged in 48 KB)
 constexpr int kMaxWorld = 8;     // GPUs of one node in the KV-slab exchange
 constexpr int kMaxSeqs = 64;     // tokens (windows) of one ragged KQKV call
 

@@ -740,93 +740,6 @@ constexpr int CMB_THREADS = 256;
 // record_out == 0: out[d] = merged, normalised attention (out = the head's output row).
 // record_out != 0: out = the head's record [kPartStride]: the merged, unnormalised record
 // (o = sum a_s o_s, m = m*, l = sum a_s l_s) -- the form that is exchanged between GPUs.
-template <int R>
-__device__ __forceinline__ void merge_head(const float* __restrict__ ph, int S, size_t ss,
-                                           float* __restrict__ out, int record_out,
-                                           float* s_alpha) {
-    __shared__ __align__(16) float s_red[CMB_THREADS / 32][128];   // written as float4
-    __shared__ float s_m[CMB_THREADS / 32], s_l[CMB_THREADS / 32];
-    const int d0 = blockIdx.y * 128;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-
-    float m = -INFINITY;
-    for (int s = tid; s < S; s += CMB_THREADS) m = fmaxf(m, __ldg(ph + s * ss + R));
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    if (lane == 0) s_m[warp] = m;
-    __syncthreads();
-    float mstar = s_m[0];
-#pragma unroll
-    for (int w = 1; w < CMB_THREADS / 32; ++w) mstar = fmaxf(mstar, s_m[w]);
-
-    float lsum = 0.0f;
-    for (int s = tid; s < S; s += CMB_THREADS) {
-        const float ms = __ldg(ph + s * ss + R);
-        const float a = (ms > -INFINITY) ? exp2f(ms - mstar) : 0.0f;
-        s_alpha[s] = a;
-        lsum += a * __ldg(ph + s * ss + (R + 1));
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
-    if (lane == 0) s_l[warp] = lsum;
-    __syncthreads();
-
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    const float* col = ph + d0 + 4 * lane;
-#pragma unroll 4
-    for (int s = warp; s < S; s += CMB_THREADS / 32) {
-        const float a = s_alpha[s];
-        const float4 v = __ldg(reinterpret_cast<const float4*>(col + s * ss));
-        acc.x = fmaf(a, v.x, acc.x);
-        acc.y = fmaf(a, v.y, acc.y);
-        acc.z = fmaf(a, v.z, acc.z);
-        acc.w = fmaf(a, v.w, acc.w);
-    }
-    *reinterpret_cast<float4*>(&s_red[warp][4 * lane]) = acc;
-    __syncthreads();
-    if (tid < 128) {
-        float o = 0.0f, l = 0.0f;
-#pragma unroll
-        for (int w = 0; w < CMB_THREADS / 32; ++w) {
-            o += s_red[w][tid];
-            l += s_l[w];
-        }
-        if (record_out) {
-            out[d0 + tid] = o;
-            if (blockIdx.y == 0 && tid == 0) {
-                out[R] = mstar;
-                out[(R + 1)] = l;
-                out[R + 2] = 0.0f;
-                out[R + 3] = 0.0f;
-            }
-        } else {
-            out[d0 + tid] = (mstar > -INFINITY) ? o / l : 0.0f;
-        }
-    }
-}
-
-// grid (32 heads, R / 128 blocks of 128 columns).  record_out: see merge_head; out_hs = the
-// output's head stride in floats (R + 4 for records).
-template <int R>
-__global__ void __launch_bounds__(CMB_THREADS)
-kqkv_combine_kernel(const float* __restrict__ part, int S, float* __restrict__ out, int64_t out_hs,
-                    int record_out) {
-    extern __shared__ float s_alpha[];   // [S]
-    pdl_wait();
-    const int h = blockIdx.x;
-    merge_head<R>(part + static_cast<size_t>(h) * (R + 4), S, static_cast<size_t>(H) * (R + 4),
-                  out + h * out_hs, record_out, s_alpha);
-}
-
-// PHASE selector 2 in one launch: the LSE merge of one head's 128-column block (merge_head's
-// arithmetic and order, so attn is bit-identical to kqkv_combine_kernel's) followed by that block's
-// share of W_UV: out[h][j] = sum over the R / 128 column blocks of sum_r W_UV[h][j][r] * f16(attn[h][r]).
-// The blocks of a head form a thread-block cluster; rank 0 adds the blocks' partial rows in rank order
-// through distributed shared memory (plain loads, no multicast), so the result is deterministic.  All
-// record loads of a warp (m, l, and up to RB records' 128 columns) are issued before the first use:
-// one L2 round trip where the two-launch form waited on several.  The block's W_UV slice (32 KB) is
-// loaded before griddepcontrol.wait, overlapping the KQKV tail.  Compared with the two launches it
-// replaces, only the order of W_UV's additions differs (per block, then across blocks).
 constexpr int CWV_RB = 19;   // records per warp in flight: 8 warps x 19 >= 148 splits
 
 __device__ __forceinline__ uint4 ldg_nc_u4(const void* p) {
@@ -853,33 +766,17 @@ __device__ __forceinline__ float butterfly_transpose_sum(float (&v)[N], int lane
     return v[0];   // lane L: the sum over its xor group of value index (L & (N - 1))
 }
 
+// Merge one head's S records over the 128 columns at d0 with every record load of a warp in flight
+// at once: merge_head's rule, order and rounding (m4-kqkv.cu:318-338; log2 units).  ph: the head's
+// first record, ss: the record stride in floats, s_ml: 2 * S floats of shared memory.  On return
+// every thread has mstar and l; threads tid < 128 have the unnormalised column sum o of column
+// d0 + tid.  Called by all CMB_THREADS threads.
 template <int R>
-__global__ void __cluster_dims__(1, R / 128, 1) __launch_bounds__(CMB_THREADS)
-kqkv_combine_wvb_kernel(const float* __restrict__ part, int S, const __half* __restrict__ w_uv,
-                        float* __restrict__ attn_out, int64_t attn_hs, float* __restrict__ out,
-                        int64_t out_hs) {
-    namespace cg = cooperative_groups;
-    extern __shared__ float s_ml[];   // [2][S]: m then alpha, l
-    __shared__ __align__(16) float s_red[CMB_THREADS / 32][128];
-    __shared__ float s_m[CMB_THREADS / 32], s_l[CMB_THREADS / 32];
-    __shared__ __align__(16) __half s_x[128];
-    __shared__ float s_part[kVHead];
-    const int h = blockIdx.x;
-    const int d0 = blockIdx.y * 128;
+__device__ __forceinline__ void merge_block_inflight(const float* __restrict__ ph, int S, size_t ss,
+                                                     int d0, float* s_ml,
+                                                     float (*s_red)[128], float* s_m, float* s_l,
+                                                     float& mstar, float& l, float& o) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const size_t ss = static_cast<size_t>(kHeads) * (R + 4);
-    const float* ph = part + static_cast<size_t>(h) * (R + 4);
-
-    // W_UV[h][j][d0 .. d0+127]: warp w holds rows 16w .. 16w+15, a half-warp one row per step
-    const int hw = lane >> 4, l16 = lane & 15;
-    uint4 wv[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        const int j = 16 * warp + 2 * k + hw;
-        wv[k] = ldg_nc_u4(w_uv + (static_cast<size_t>(h) * kVHead + j) * R + d0 + 8 * l16);
-    }
-    pdl_wait();
-
     float4 ov[CWV_RB];
     auto load_records = [&](int sb) {
 #pragma unroll
@@ -903,7 +800,7 @@ kqkv_combine_wvb_kernel(const float* __restrict__ part, int S, const __half* __r
     for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
     if (lane == 0) s_m[warp] = m;
     __syncthreads();
-    float mstar = s_m[0];
+    mstar = s_m[0];
 #pragma unroll
     for (int w = 1; w < CMB_THREADS / 32; ++w) mstar = fmaxf(mstar, s_m[w]);
     float lsum = 0.0f;
@@ -937,13 +834,93 @@ kqkv_combine_wvb_kernel(const float* __restrict__ part, int S, const __half* __r
     }
     *reinterpret_cast<float4*>(&s_red[warp][4 * lane]) = acc;
     __syncthreads();
-    if (tid < 128) {
-        float o = 0.0f, l = 0.0f;
+    o = 0.0f;
+    l = 0.0f;
 #pragma unroll
-        for (int w = 0; w < CMB_THREADS / 32; ++w) {
-            o += s_red[w][tid];
-            l += s_l[w];
+    for (int w = 0; w < CMB_THREADS / 32; ++w) l += s_l[w];
+    if (tid < 128) {
+#pragma unroll
+        for (int w = 0; w < CMB_THREADS / 32; ++w) o += s_red[w][tid];
+    }
+}
+
+template <int R>
+__device__ __forceinline__ void merge_head(const float* __restrict__ ph, int S, size_t ss,
+                                           float* __restrict__ out, int record_out,
+                                           float* s_ml) {
+    __shared__ __align__(16) float s_red[CMB_THREADS / 32][128];   // written as float4
+    __shared__ float s_m[CMB_THREADS / 32], s_l[CMB_THREADS / 32];
+    const int d0 = blockIdx.y * 128;
+    const int tid = threadIdx.x;
+    float mstar, l, o;
+    merge_block_inflight<R>(ph, S, ss, d0, s_ml, s_red, s_m, s_l, mstar, l, o);
+    if (tid < 128) {
+        if (record_out) {
+            out[d0 + tid] = o;
+            if (blockIdx.y == 0 && tid == 0) {
+                out[R] = mstar;
+                out[(R + 1)] = l;
+                out[R + 2] = 0.0f;
+                out[R + 3] = 0.0f;
+            }
+        } else {
+            out[d0 + tid] = (mstar > -INFINITY) ? o / l : 0.0f;
         }
+    }
+}
+
+// grid (32 heads, R / 128 blocks of 128 columns).  record_out: see merge_head; out_hs = the
+// output's head stride in floats (R + 4 for records).
+template <int R>
+__global__ void __launch_bounds__(CMB_THREADS)
+kqkv_combine_kernel(const float* __restrict__ part, int S, float* __restrict__ out, int64_t out_hs,
+                    int record_out) {
+    extern __shared__ float s_ml[];   // [2][S]
+    pdl_wait();
+    const int h = blockIdx.x;
+    merge_head<R>(part + static_cast<size_t>(h) * (R + 4), S, static_cast<size_t>(H) * (R + 4),
+                  out + h * out_hs, record_out, s_ml);
+}
+
+// PHASE selector 2 in one launch: the LSE merge of one head's 128-column block (merge_head's
+// arithmetic and order, so attn is bit-identical to kqkv_combine_kernel's) followed by that block's
+// share of W_UV: out[h][j] = sum over the R / 128 column blocks of sum_r W_UV[h][j][r] * f16(attn[h][r]).
+// The blocks of a head form a thread-block cluster; rank 0 adds the blocks' partial rows in rank order
+// through distributed shared memory (plain loads, no multicast), so the result is deterministic.  All
+// record loads of a warp (m, l, and up to RB records' 128 columns) are issued before the first use:
+// one L2 round trip where the two-launch form waited on several.  The block's W_UV slice (32 KB) is
+// loaded before griddepcontrol.wait, overlapping the KQKV tail.  Compared with the two launches it
+// replaces, only the order of W_UV's additions differs (per block, then across blocks).
+template <int R>
+__global__ void __cluster_dims__(1, R / 128, 1) __launch_bounds__(CMB_THREADS)
+kqkv_combine_wvb_kernel(const float* __restrict__ part, int S, const __half* __restrict__ w_uv,
+                        float* __restrict__ attn_out, int64_t attn_hs, float* __restrict__ out,
+                        int64_t out_hs) {
+    namespace cg = cooperative_groups;
+    extern __shared__ float s_ml[];   // [2][S]: m then alpha, l
+    __shared__ __align__(16) float s_red[CMB_THREADS / 32][128];
+    __shared__ float s_m[CMB_THREADS / 32], s_l[CMB_THREADS / 32];
+    __shared__ __align__(16) __half s_x[128];
+    __shared__ float s_part[kVHead];
+    const int h = blockIdx.x;
+    const int d0 = blockIdx.y * 128;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t ss = static_cast<size_t>(kHeads) * (R + 4);
+    const float* ph = part + static_cast<size_t>(h) * (R + 4);
+
+    // W_UV[h][j][d0 .. d0+127]: warp w holds rows 16w .. 16w+15, a half-warp one row per step
+    const int hw = lane >> 4, l16 = lane & 15;
+    uint4 wv[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int j = 16 * warp + 2 * k + hw;
+        wv[k] = ldg_nc_u4(w_uv + (static_cast<size_t>(h) * kVHead + j) * R + d0 + 8 * l16);
+    }
+    pdl_wait();
+
+    float mstar, l, o;
+    merge_block_inflight<R>(ph, S, ss, d0, s_ml, s_red, s_m, s_l, mstar, l, o);
+    if (tid < 128) {
         const float at = (mstar > -INFINITY) ? o / l : 0.0f;
         if (attn_out != nullptr) attn_out[h * attn_hs + d0 + tid] = at;
         s_x[tid] = __float2half_rn(at);
@@ -999,7 +976,7 @@ __global__ void __launch_bounds__(CMB_THREADS)
 kqkv_ragged_combine_kernel(const float* __restrict__ part, const int32_t* __restrict__ seq_base,
                            const int32_t* __restrict__ seq_len, int n_seq, int n_rows, int G,
                            float* __restrict__ out, int64_t out_hs, int64_t out_ts) {
-    __shared__ float s_alpha[kMaxSplits];
+    __shared__ float s_ml[2 * kMaxSplits];
     __shared__ int s_first, s_count;
     pdl_wait();
     const int h = blockIdx.x;
@@ -1027,7 +1004,7 @@ kqkv_ragged_combine_kernel(const float* __restrict__ part, const int32_t* __rest
     }
     const size_t ss = static_cast<size_t>(H) * (R + 4);
     merge_head<R>(part + static_cast<size_t>(s_first + t) * ss + static_cast<size_t>(h) * (R + 4),
-                  s_count, ss, orow, 0, s_alpha);
+                  s_count, ss, orow, 0, s_ml);
 }
 
 }  // namespace kq
@@ -1095,8 +1072,8 @@ cudaError_t launch_kqkv_partials(const KqkvLaunch& a, cudaStream_t stream) {
 
 cudaError_t launch_kqkv_combine(const float* part, int S, int latent, float* out, int64_t out_hs,
                                 uint32_t flags, cudaStream_t stream) {
-    const size_t smem = static_cast<size_t>(S) * sizeof(float);
-    if (smem > 48 * 1024) return note(cudaErrorInvalidValue);   // > 12288 records: not a config
+    const size_t smem = 2 * static_cast<size_t>(S) * sizeof(float);
+    if (smem > 48 * 1024) return note(cudaErrorInvalidValue);   // > 6144 records: not a config
     if (latent == 256)
         return launch(kq::kqkv_combine_kernel<256>, dim3(kHeads, 2), dim3(kq::CMB_THREADS), smem,
                       stream, flags, part, S, out, out_hs, 0);
@@ -1129,7 +1106,7 @@ cudaError_t launch_kqkv_ragged_combine(const float* part, const int32_t* seq_bas
 
 cudaError_t launch_kqkv_merge_records(const float* part, int S, int latent, float* out_records,
                                       uint32_t flags, cudaStream_t stream) {
-    const size_t smem = static_cast<size_t>(S) * sizeof(float);
+    const size_t smem = 2 * static_cast<size_t>(S) * sizeof(float);
     if (smem > 48 * 1024) return note(cudaErrorInvalidValue);
     if (latent == 256)
         return launch(kq::kqkv_combine_kernel<256>, dim3(kHeads, 2), dim3(kq::CMB_THREADS), smem,

@@ -184,8 +184,8 @@ M4B_API int m4b_kqkv_static_scratch(const m4b_kqkv_args * args, m4b_stream_t str
  *                       stride); dst F32 [128, T, 32].  T = 1 in the reference's op; additively
  *                       1 <= T <= 64 tokens (token stride nb[1]) share one read of W_UV
  *   phase 2  COMBINE_WVB (additive selector): src0 W_UV F16 [512, 128, 32]; src1 partials
- *                       F32 [516, 32, S] (m4b_kqkv_partials layout, any S >= 1, e.g. gathered
- *                       from several GPUs); dst F32 [128, 1, 32]; optional src2 F32
+ *                       F32 [516, 32, S] (m4b_kqkv_partials layout, 1 <= S <= 6144, e.g.
+ *                       gathered from several GPUs); dst F32 [128, 1, 32]; optional src2 F32
  *                       [512, 1, 32] receives the merged attention output.  Needs scratch
  *                       >= m4b_phase_scratch_bytes(2) unless src2 is given.
  *   phase 3  MERGE      (additive selector): src1 partial records F32 [516, 32, S]; dst F32
