@@ -223,6 +223,142 @@ gather_wvb_kernel(char* __restrict__ local, int world, Layout L, const __half* _
     }
 }
 
+// The whole exchange in one launch: per head h and 128-column block (a cluster of the head's
+// blocks, as in kqkv_combine_wvb_kernel) -- merge this GPU's S split records (publish_kernel's
+// arithmetic), store the block, epoch-tagged, into slot [rank] of every GPU's receive buffer, wait
+// (bounded) for every GPU's block of the same exchange, merge those `world` records and normalise
+// (gather_wvb_kernel's arithmetic: attn is bit-identical to the two-launch form), then apply the
+// block's W_UV slice and add the cluster's partial rows in rank order through distributed shared
+// memory.  A block waits only for the same block of the other GPUs, which never waits for anything
+// before publishing, so the waits always end.
+__global__ void __cluster_dims__(1, kLatent / 128, 1) __launch_bounds__(THREADS)
+merge_exchange_wvb_kernel(const float* __restrict__ part, int S, PeerPtrs peers, char* local,
+                          int world, int rank, Layout L, const __half* __restrict__ w_uv,
+                          float* __restrict__ attn_out, int64_t attn_hs, float* __restrict__ out,
+                          int64_t out_hs) {
+    namespace cg = cooperative_groups;
+    extern __shared__ float s_ml[];   // [2][S]
+    __shared__ __align__(16) float s_red[THREADS / 32][128];
+    __shared__ float s_m[THREADS / 32], s_l[THREADS / 32];
+    __shared__ float s_wm[kMaxWorld], s_wl[kMaxWorld];
+    __shared__ __align__(16) __half s_x[128];
+    __shared__ float s_part[kVHead];
+    const int h = blockIdx.x;
+    const int d0 = blockIdx.y * 128;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int hw = lane >> 4, l16 = lane & 15;
+
+    uint4 wv[8];   // W_UV[h][j][d0 .. d0+127], rows 16 * warp .. + 15 (no dependency on earlier kernels)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int j = 16 * warp + 2 * k + hw;
+        wv[k] = kq::ldg_nc_u4(w_uv + (static_cast<size_t>(h) * kVHead + j) * kLatent + d0 + 8 * l16);
+    }
+    pdl_wait();
+    const uint64_t e = *reinterpret_cast<volatile uint64_t*>(local + L.epoch_off) + 1;
+    const uint32_t e32 = static_cast<uint32_t>(e);
+
+    // 1. this GPU's record block, stored into every GPU's slot [rank]
+    {
+        const size_t ss = static_cast<size_t>(kHeads) * kPartStride;
+        float mstar, l, o;
+        kq::merge_block_inflight<kLatent>(part + static_cast<size_t>(h) * kPartStride, S, ss, d0,
+                                          s_ml, s_red, s_m, s_l, mstar, l, o);
+        if (tid < 128) {
+#pragma unroll
+            for (int p = 0; p < kMaxWorld; ++p) {
+                if (p >= world) break;
+                uint64_t* rec = record(peers.p[p], L, e, world, rank, h);
+                st_word(rec + d0 + tid, o, e32);
+                if (tid == 0) {   // every block carries m and l: no block waits for another's
+                    st_word(rec + kPartM, mstar, e32);
+                    st_word(rec + kPartL, l, e32);
+                }
+            }
+        }
+    }
+
+    // 2. every GPU's block of this exchange (bounded polls of the epoch in each word)
+    const long long t0 = clock64();
+    if (tid < world) {
+        const uint64_t* rec = record(local, L, e, world, tid, h);
+        s_wm[tid] = ld_word(rec + kPartM, e32, t0);
+        s_wl[tid] = ld_word(rec + kPartL, e32, t0);
+    }
+    float v[kMaxWorld];
+    if (tid < 128) {
+#pragma unroll
+        for (int r = 0; r < kMaxWorld; ++r)
+            if (r < world) v[r] = ld_word(record(local, L, e, world, r, h) + d0 + tid, e32, t0);
+    }
+    __syncthreads();
+    if (tid < 128) {
+        float mstar = -INFINITY;
+        for (int r = 0; r < world; ++r) mstar = fmaxf(mstar, s_wm[r]);
+        float l = 0.0f, o = 0.0f;
+#pragma unroll
+        for (int r = 0; r < kMaxWorld; ++r) {
+            if (r < world) {
+                const float a = (s_wm[r] > -INFINITY) ? exp2f(s_wm[r] - mstar) : 0.0f;
+                l = fmaf(a, s_wl[r], l);
+                o = fmaf(a, v[r], o);
+            }
+        }
+        const float inv = (mstar > -INFINITY && l > 0.0f) ? 1.0f / l : 0.0f;
+        const float x = (inv != 0.0f) ? o * inv : 0.0f;
+        if (attn_out != nullptr) attn_out[h * attn_hs + d0 + tid] = x;
+        s_x[tid] = __float2half_rn(x);
+    }
+    __syncthreads();
+
+    // 3. the block's share of W_UV, summed over the cluster in rank order
+    float xf[8];
+    {
+        const uint4 xu = *reinterpret_cast<const uint4*>(s_x + 8 * l16);
+        const __half2* x2 = reinterpret_cast<const __half2*>(&xu);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(x2[i]);
+            xf[2 * i] = f.x;
+            xf[2 * i + 1] = f.y;
+        }
+    }
+    float dots[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const __half2* w2 = reinterpret_cast<const __half2*>(&wv[k]);
+        float a = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(w2[i]);
+            a = fmaf(f.x, xf[2 * i], a);
+            a = fmaf(f.y, xf[2 * i + 1], a);
+        }
+        dots[k] = a;
+    }
+    float r = kq::butterfly_transpose_sum<8>(dots, lane);
+    r += __shfl_xor_sync(0xffffffffu, r, 8);
+    if ((l16 & 8) == 0) s_part[16 * warp + 2 * l16 + hw] = r;
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    if (cluster.block_rank() == 0 && tid < kVHead) {
+        float o = 0.0f;
+#pragma unroll
+        for (int b = 0; b < kLatent / 128; ++b) o += cluster.map_shared_rank(s_part, b)[tid];
+        out[h * out_hs + tid] = o;
+    }
+    cluster.sync();
+
+    // 4. the epoch advances once every block has read it
+    if (tid == 0) {
+        unsigned* arrive = reinterpret_cast<unsigned*>(local + L.arrive_off);
+        if (atomicAdd(arrive, 1u) == gridDim.x * gridDim.y - 1) {
+            *arrive = 0;
+            *reinterpret_cast<volatile uint64_t*>(local + L.epoch_off) = e;
+        }
+    }
+}
+
 }  // namespace xch
 }  // namespace m4b
 
@@ -346,6 +482,41 @@ M4B_API int m4b_exchange_combine_wvb(m4b_exchange* x, const m4b_phase_args* a,
     return status_of(launch(xch::gather_wvb_kernel, dim3(kHeads, kVHead / xch::GW_ROWS),
                             dim3(xch::THREADS), 0, reinterpret_cast<cudaStream_t>(stream), a->flags,
                             x->local, x->world, xch::layout(x->world),
+                            static_cast<const __half*>(a->src[0].data), attn, attn_hs,
+                            static_cast<float*>(a->dst.data),
+                            static_cast<int64_t>(a->dst.nb[2] / 4)));
+}
+
+M4B_API int m4b_exchange_merge_wvb(m4b_exchange* x, const m4b_phase_args* a,
+                                   m4b_stream_t stream) {
+    if (!x || !a) return M4B_EINVAL;
+    for (int r = 0; r < x->world; ++r)
+        if (!x->peer[r]) return M4B_EINVAL;   // m4b_exchange_open not done
+    int geom = 0;
+    int rc = check_wuv(a->src[0], &geom);
+    if (rc != M4B_OK) return rc;
+    if (geom != kGeomBaseline) return M4B_ENOTSUP;   // the exchange carries 516-float records
+    rc = check_partials(a->src[1], kMaxRecords, kGeomBaseline);
+    if (rc != M4B_OK) return rc;
+    rc = check_phase_dst(a->dst);
+    if (rc != M4B_OK) return rc;
+    float* attn = nullptr;
+    int64_t attn_hs = kLatent;
+    if (a->src[2].data != nullptr) {
+        if (check_attn(a->src[2], kGeomBaseline) != M4B_OK) return M4B_EINVAL;
+        attn = static_cast<float*>(a->src[2].data);
+        attn_hs = static_cast<int64_t>(a->src[2].nb[2] / 4);
+    }
+    rc = device_check(nullptr);
+    if (rc != M4B_OK) return rc;
+    xch::PeerPtrs pp;
+    for (int r = 0; r < kMaxWorld; ++r) pp.p[r] = r < x->world ? x->peer[r] : nullptr;
+    const int S = static_cast<int>(a->src[1].ne[2]);
+    const size_t smem = 2 * static_cast<size_t>(S) * sizeof(float);
+    return status_of(launch(xch::merge_exchange_wvb_kernel, dim3(kHeads, kLatent / 128),
+                            dim3(xch::THREADS), smem, reinterpret_cast<cudaStream_t>(stream),
+                            a->flags, static_cast<const float*>(a->src[1].data), S, pp, x->local,
+                            x->world, x->rank, xch::layout(x->world),
                             static_cast<const __half*>(a->src[0].data), attn, attn_hs,
                             static_cast<float*>(a->dst.data),
                             static_cast<int64_t>(a->dst.nb[2] / 4)));

@@ -30,6 +30,8 @@ _lib.m4b_exchange_destroy.argtypes = [ctypes.c_void_p]
 _lib.m4b_exchange_publish.argtypes = [ctypes.c_void_p, ctypes.POINTER(m4.PhaseArgs), ctypes.c_void_p]
 _lib.m4b_exchange_combine_wvb.argtypes = [ctypes.c_void_p, ctypes.POINTER(m4.PhaseArgs),
                                           ctypes.c_void_p]
+_lib.m4b_exchange_merge_wvb.argtypes = [ctypes.c_void_p, ctypes.POINTER(m4.PhaseArgs),
+                                         ctypes.c_void_p]
 
 
 class PeerExchange:
@@ -63,6 +65,20 @@ class PeerExchange:
         a.flags = flags
         m4._check(_lib.m4b_exchange_combine_wvb(self._h, ctypes.byref(a), m4._stream()),
                   "m4b_exchange_combine_wvb")
+        return out
+
+    def merge_wvb(self, partials: torch.Tensor, w_uv: torch.Tensor, out: torch.Tensor,
+                  attn_out: torch.Tensor | None = None, flags: int = 0) -> torch.Tensor:
+        """publish + combine_wvb in one launch (m4b_exchange_merge_wvb)."""
+        a = m4.PhaseArgs()
+        a.src[0] = m4.gtensor(w_uv, list(reversed(w_uv.shape)))
+        a.src[1] = m4.gtensor(partials, [m4.PART_STRIDE, m4.HEADS, partials.shape[0], 1])
+        if attn_out is not None:
+            a.src[2] = m4._heads_desc(attn_out, m4.LATENT)
+        a.dst = m4._heads_desc(out, m4.VHEAD)
+        a.flags = flags
+        m4._check(_lib.m4b_exchange_merge_wvb(self._h, ctypes.byref(a), m4._stream()),
+                  "m4b_exchange_merge_wvb")
         return out
 
     def close(self, group=None) -> None:

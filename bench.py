@@ -264,9 +264,8 @@ def slab_workload(args, rank, world, dev):
             m4.wkb(wuk[layer], q[layer][:, :NOPE], out=qcur[layer][:, :R], flags=flags)
             m4.kqkv_partials(kc[layer], qcur[layer], None, SCALE, out=part,
                              flags=flags | m4.FLAG_KV_STATIC)
-            if xchg is not None:   # fused: merge + NVLink stores into every peer, then wait+merge
-                xchg.publish(part, flags=flags)
-                xchg.combine_wvb(wuv[layer], out=w.out[layer], attn_out=attn, flags=flags)
+            if xchg is not None:   # one launch: merge, NVLink stores into every peer, wait, merge, W_UV
+                xchg.merge_wvb(part, wuv[layer], out=w.out[layer], attn_out=attn, flags=flags)
                 continue
             if world > 1:   # library collective: merge the local splits, all-gather 66 KB per rank
                 m4.phase_merge_records(part, out=merged, flags=flags)
@@ -282,7 +281,9 @@ def slab_workload(args, rank, world, dev):
     w.kq_kernel = "kqkv_partial_kernel"
     w.kq_bytes = 1152 * n_loc + H * D * 4
     w.job_layer_bytes = layer_bytes(N)
-    w.launches_per_step = (4 if (world == 1 or xchg is not None) else 5) * L
+    # WKB, partials, merge + W_UV (one launch; with the fused exchange, the exchange too); the
+    # NCCL variant adds the local record merge (NCCL's own kernel is not counted)
+    w.launches_per_step = (3 if (world == 1 or xchg is not None) else 4) * L
     w.traffic = profiled_traffic("kqkv_partial_n262144.md")
     if w.traffic is not None and world > 1:
         w.traffic = w.traffic / world        # the committed capture is of the 1-GPU slab

@@ -238,6 +238,10 @@ M4B_API int m4b_exchange_destroy(m4b_exchange * x);
 M4B_API int m4b_exchange_publish(m4b_exchange * x, const m4b_phase_args * args, m4b_stream_t stream);
 M4B_API int m4b_exchange_combine_wvb(m4b_exchange * x, const m4b_phase_args * args,
                                      m4b_stream_t stream);
+/* publish + combine_wvb in one launch: src[0] W_UV, src[1] this GPU's records [516, 32, S],
+ * optional src[2] attention output, dst as combine_wvb.  Every GPU calls it once per exchange. */
+M4B_API int m4b_exchange_merge_wvb(m4b_exchange * x, const m4b_phase_args * args,
+                                   m4b_stream_t stream);
 
 /* Sizes.  geometry: 0 = BASELINE, 1 = MISTRAL_SMALL. */
 M4B_API uint64_t m4b_kqkv_scratch_bytes(int geometry, int64_t n_kv);

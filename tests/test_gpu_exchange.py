@@ -3,7 +3,8 @@ contiguous slab of the cache, computes split-K records over it, publishes one me
 head into every peer over NVLink and merges all ranks' records before W_UV.  The result must
 match the oracle's single-GPU layer step on the whole cache (the reference runs on one GPU,
 engine/m1_engine.cpp:2165).  Covers repeated exchanges (the double-buffered receive halves),
-a CUDA-graph replay of several layers, and a mask under which one rank's slab is fully masked.
+a CUDA-graph replay of several layers, a mask under which one rank's slab is fully masked, and the
+one-launch form of the exchange (m4b_exchange_merge_wvb) against the two-launch form.
 
 Needs at least 2 GPUs; skipped otherwise.  Handles travel over a gloo group on 127.0.0.1; the
 data path uses no library collective.
@@ -72,37 +73,41 @@ def _worker(rank, world, port, out_dir):
     attn = torch.empty(len(layers), G.H, G.R, device=dev)
     out = torch.empty(len(layers), G.H, G.V, device=dev)
 
-    def layer_step(i, flags):
+    def layer_step(i, flags, fused):
         L = layers[i]
         m4.wkb(L["w_uk"], L["q"][:, :G.nope], out=L["qcur"][:, :G.R], flags=flags)
         m4.kqkv_partials(L["kc"], L["qcur"], L["mask"], G.scale, out=part, flags=flags)
-        x.publish(part, flags=flags)
-        x.combine_wvb(L["w_uv"], out=out[i], attn_out=attn[i], flags=flags)
+        if fused:   # one launch: merge, publish, wait, merge, W_UV
+            x.merge_wvb(part, L["w_uv"], out=out[i], attn_out=attn[i], flags=flags)
+        else:
+            x.publish(part, flags=flags)
+            x.combine_wvb(L["w_uv"], out=out[i], attn_out=attn[i], flags=flags)
 
     results = {}
-    dist.barrier()
-    # eager: 7 exchanges cycle both receive halves several times; keep the last result per layer
-    for k in range(7):
-        layer_step(k % 3, 0)
-    torch.cuda.synchronize()
-    results["eager_attn"], results["eager_out"] = attn.cpu().numpy(), out.cpu().numpy()
-    attn.zero_()
-    out.zero_()
-    # one CUDA graph over the three layers with PDL, replayed three times
-    s = torch.cuda.Stream()
-    s.wait_stream(torch.cuda.current_stream())
-    torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=s):
-        for i in range(3):
-            layer_step(i, m4.FLAG_PDL)
-    dist.barrier()
-    for _ in range(3):
-        g.replay()
-    torch.cuda.synchronize()
-    results["graph_attn"], results["graph_out"] = attn.cpu().numpy(), out.cpu().numpy()
+    for mode, fused in (("two", False), ("one", True)):   # both share the exchange's epochs
+        dist.barrier()
+        # eager: 7 exchanges cycle both receive halves; keep the last result per layer
+        for k in range(7):
+            layer_step(k % 3, 0, fused)
+        torch.cuda.synchronize()
+        results[f"{mode}_eager_attn"], results[f"{mode}_eager_out"] = attn.cpu().numpy(), out.cpu().numpy()
+        attn.zero_()
+        out.zero_()
+        # one CUDA graph over the three layers with PDL, replayed three times
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(3):
+                layer_step(i, m4.FLAG_PDL, fused)
+        dist.barrier()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        results[f"{mode}_graph_attn"], results[f"{mode}_graph_out"] = attn.cpu().numpy(), out.cpu().numpy()
+        del g
     results["status"] = np.array(m4.device_status())
-    del g
     x.close()
     np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **results)
     dist.barrier()
@@ -122,7 +127,12 @@ def test_exchange_matches_single_gpu_oracle(tmp_path, world):
     for r in range(world):
         res = np.load(tmp_path / f"rank{r}.npz")
         assert int(res["status"]) == 0, f"rank {r}: device status {int(res['status'])}"
+        for mode in ("two", "one"):
+            for kind in ("eager", "graph"):
+                for i, (a, o) in enumerate(refs):
+                    assert rel_to_max(res[f"{mode}_{kind}_attn"][i], a) <= ATTN_TOL, (r, mode, kind, i)
+                    assert rel_to_max(res[f"{mode}_{kind}_out"][i], o) <= ATTN_TOL, (r, mode, kind, i)
+        # the one-launch exchange merges with the two launches' arithmetic; only W_UV's order differs
         for kind in ("eager", "graph"):
-            for i, (a, o) in enumerate(refs):
-                assert rel_to_max(res[f"{kind}_attn"][i], a) <= ATTN_TOL, (r, kind, i)
-                assert rel_to_max(res[f"{kind}_out"][i], o) <= ATTN_TOL, (r, kind, i)
+            assert np.array_equal(res[f"one_{kind}_attn"], res[f"two_{kind}_attn"]), (r, kind)
+            assert rel_to_max(res[f"one_{kind}_out"], res[f"two_{kind}_out"]) <= 1e-5, (r, kind)
