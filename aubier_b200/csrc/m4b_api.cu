@@ -348,6 +348,39 @@ void yarn_corr_dims(int n_dims, int n_ctx_orig, float base, float beta_fast, flo
     *hi = std::min(static_cast<float>(n_dims - 1), ceilf(b));
 }
 
+// PHASE selector 0 on a validated argument block (slab: see KvWriteLaunch).
+int kvwrite(const m4b_phase_args& pa, int slab, int64_t slab_base, cudaStream_t s) {
+    const m4b_phase_args* a = &pa;
+    float* out = static_cast<float*>(a->dst.data);
+    KvWriteLaunch k;
+    k.cur = static_cast<const float*>(a->src[0].data);
+    k.w = a->src[1].data;
+    k.norm_w = static_cast<const float*>(a->src[2].data);
+    k.kcache = a->src[3].data;
+    k.kcache_row_stride = static_cast<int64_t>(a->src[3].nb[1] / 2);
+    k.kcache_rows = a->src[3].ne[1];
+    k.kidx = static_cast<const int64_t*>(a->src[4].data);
+    k.pos = static_cast<const int32_t*>(a->src[5].data);
+    k.kcur = out;
+    // op_params (ggml.c:3464-3468, an int32 array): [1] freq_base [2] freq_scale
+    // [3] ext_factor [4] attn_factor [5] beta_fast [6] beta_slow [7] eps [8] n_dims
+    // [9] n_ctx_orig
+    const float freq_base = param_f32(a->op_params, 1);
+    k.freq_scale = param_f32(a->op_params, 2);
+    k.ext_factor = param_f32(a->op_params, 3);
+    k.attn_factor = param_f32(a->op_params, 4);
+    const float beta_fast = param_f32(a->op_params, 5);
+    const float beta_slow = param_f32(a->op_params, 6);
+    k.eps = param_f32(a->op_params, 7);
+    const int n_dims = a->op_params[8];
+    yarn_corr_dims(n_dims, a->op_params[9], freq_base, beta_fast, beta_slow, &k.corr0, &k.corr1);
+    k.theta_scale = powf(freq_base, -2.0f / static_cast<float>(n_dims));
+    k.flags = a->flags;
+    k.slab = slab;
+    k.slab_base = slab_base;
+    return status_of(launch_kvwrite(k, s));
+}
+
 }  // namespace
 }  // namespace m4b
 
@@ -401,6 +434,9 @@ int m4b_wkb(const m4b_wkb_args* a, m4b_stream_t stream) {
     int geom = 0;
     int rc = check_wkb(a->src0, a->src1, a->dst, &geom);
     if (rc != M4B_OK) return rc;
+    if ((a->flags & M4B_FLAG_QCAT) &&   // the rope half sits after q_nope / after the latent
+        (a->src1.nb[1] < 4u * (kGeo[geom].nope + 64) || a->dst.nb[1] < 4u * (kGeo[geom].latent + 64)))
+        return M4B_EINVAL;
     rc = device_check(nullptr);
     if (rc != M4B_OK) return rc;
     const Rows qr = {static_cast<int64_t>(a->src1.nb[1] / 4), static_cast<int64_t>(a->src1.nb[2] / 4)};
@@ -517,33 +553,7 @@ int m4b_phase(const m4b_phase_args* a, m4b_stream_t stream) {
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     float* out = static_cast<float*>(a->dst.data);
     const int64_t out_hs = static_cast<int64_t>(a->dst.nb[2] / 4);
-    if (phase == 0) {
-        KvWriteLaunch k;
-        k.cur = static_cast<const float*>(a->src[0].data);
-        k.w = a->src[1].data;
-        k.norm_w = static_cast<const float*>(a->src[2].data);
-        k.kcache = a->src[3].data;
-        k.kcache_row_stride = static_cast<int64_t>(a->src[3].nb[1] / 2);
-        k.kcache_rows = a->src[3].ne[1];
-        k.kidx = static_cast<const int64_t*>(a->src[4].data);
-        k.pos = static_cast<const int32_t*>(a->src[5].data);
-        k.kcur = out;
-        // op_params (ggml.c:3464-3468, an int32 array): [1] freq_base [2] freq_scale
-        // [3] ext_factor [4] attn_factor [5] beta_fast [6] beta_slow [7] eps [8] n_dims
-        // [9] n_ctx_orig
-        const float freq_base = param_f32(a->op_params, 1);
-        k.freq_scale = param_f32(a->op_params, 2);
-        k.ext_factor = param_f32(a->op_params, 3);
-        k.attn_factor = param_f32(a->op_params, 4);
-        const float beta_fast = param_f32(a->op_params, 5);
-        const float beta_slow = param_f32(a->op_params, 6);
-        k.eps = param_f32(a->op_params, 7);
-        const int n_dims = a->op_params[8];
-        yarn_corr_dims(n_dims, a->op_params[9], freq_base, beta_fast, beta_slow, &k.corr0, &k.corr1);
-        k.theta_scale = powf(freq_base, -2.0f / static_cast<float>(n_dims));
-        k.flags = a->flags;
-        return status_of(launch_kvwrite(k, s));
-    }
+    if (phase == 0) return kvwrite(*a, 0, 0, s);
     if (phase == 3) {
         return status_of(launch_kqkv_merge_records(static_cast<const float*>(a->src[1].data),
                                                    static_cast<int>(a->src[1].ne[2]),
@@ -574,6 +584,16 @@ int m4b_phase(const m4b_phase_args* a, m4b_stream_t stream) {
                                         attn_hs, a->flags & M4B_FLAG_PDL, s);
     if (e != cudaSuccess) return M4B_ECUDA;
     return status_of(wvb(attn, Rows{attn_hs, 0}, Rows{out_hs, 0}, 1, a->flags & M4B_FLAG_PDL));
+}
+
+int m4b_phase_kvwrite_slab(const m4b_phase_args* a, int64_t slab_base, m4b_stream_t stream) {
+    if (!a || a->op_params[0] != 0 || slab_base < 0) return M4B_EINVAL;
+    int geom = 0;
+    int rc = check_phase(*a, &geom);
+    if (rc != M4B_OK) return rc;
+    rc = device_check(nullptr);
+    if (rc != M4B_OK) return rc;
+    return kvwrite(*a, 1, slab_base, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int m4b_supports_op(int op, const m4b_tensor* srcs, int n_srcs, const m4b_tensor* dst,

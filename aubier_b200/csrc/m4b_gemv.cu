@@ -52,7 +52,7 @@ constexpr int WKB_THREADS = 256;
 
 __global__ void __launch_bounds__(WKB_THREADS)
 wkb_f16_kernel(const __half* __restrict__ w, const float* __restrict__ q, Rows qr,
-               float* __restrict__ out, Rows outr, int nt) {
+               float* __restrict__ out, Rows outr, int nt, int qcat) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int row0 = (blockIdx.x * (WKB_THREADS / 32) + warp) * WKB_ROWS_PER_WARP;
@@ -69,6 +69,11 @@ wkb_f16_kernel(const __half* __restrict__ w, const float* __restrict__ q, Rows q
     }
     pdl_launch_dependents();
     pdl_wait();
+    if (qcat) {   // the kLatent / 64 CTAs of head h share its tokens
+        constexpr int per_head = kLatent / (WKB_ROWS_PER_WARP * (WKB_THREADS / 32));
+        wkb_concat_rope(q, qr, kNope, out, outr, kLatent, nt, h, blockIdx.x % per_head, per_head,
+                        WKB_THREADS);
+    }
     for (int t = 0; t < nt; ++t) {
         const float* qt = q + t * qr.ts + h * qr.hs + 8 * l16;
         float qf[8];
@@ -201,7 +206,7 @@ constexpr int WVB_TCH = 16;   // 2 rows x 16 tokens = 32 values, 32 lanes
 
 __global__ void __launch_bounds__(WKB_THREADS)
 wkb_f16_batch_kernel(const __half* __restrict__ w, const float* __restrict__ q, Rows qr,
-                     float* __restrict__ out, Rows outr, int nt) {
+                     float* __restrict__ out, Rows outr, int nt, int qcat) {
     extern __shared__ __align__(16) uint8_t dyn_smem[];
     __half* xs = reinterpret_cast<__half*>(dyn_smem);   // [ntp][kNope]
     const int warp = threadIdx.x >> 5;
@@ -219,6 +224,11 @@ wkb_f16_batch_kernel(const __half* __restrict__ w, const float* __restrict__ q, 
         wv[it] = ldg_stream(w + static_cast<size_t>(row0 + 2 * it + hw) * kNope + 8 * l16);
     pdl_launch_dependents();
     pdl_wait();
+    if (qcat) {   // the kLatent / 64 CTAs of head h share its tokens
+        constexpr int per_head = kLatent / (WKB_ROWS_PER_WARP * (WKB_THREADS / 32));
+        wkb_concat_rope(q, qr, kNope, out, outr, kLatent, nt, h, blockIdx.x % per_head, per_head,
+                        WKB_THREADS);
+    }
     stage_tokens(xs, q, qr, h, nt, ntp, kNope / 8, WKB_THREADS);
     float wf[WKB_ROWS_PER_WARP / 2][8];
 #pragma unroll
@@ -299,6 +309,7 @@ wvb_f16_batch_kernel(const __half* __restrict__ w, const float* __restrict__ x, 
 cudaError_t launch_wkb_f16(const void* w, const float* q, Rows qr, float* out, Rows outr, int nt,
                            uint32_t flags, cudaStream_t stream) {
     using namespace gemv;
+    const int qcat = (flags & M4B_FLAG_QCAT) ? 1 : 0;
     constexpr int rows = kHeads * kLatent;
     constexpr int grid = rows / (WKB_ROWS_PER_WARP * (WKB_THREADS / 32));
     static_assert(kLatent % (WKB_ROWS_PER_WARP * (WKB_THREADS / 32)) == 0, "a CTA spans one head");
@@ -306,10 +317,10 @@ cudaError_t launch_wkb_f16(const void* w, const float* q, Rows qr, float* out, R
         const int ntp = (nt + WKB_TCH - 1) / WKB_TCH * WKB_TCH;
         return launch(wkb_f16_batch_kernel, dim3(grid), dim3(WKB_THREADS),
                       static_cast<size_t>(ntp) * kNope * sizeof(__half), stream, flags,
-                      static_cast<const __half*>(w), q, qr, out, outr, nt);
+                      static_cast<const __half*>(w), q, qr, out, outr, nt, qcat);
     }
     return launch(wkb_f16_kernel, dim3(grid), dim3(WKB_THREADS), 0, stream, flags,
-                  static_cast<const __half*>(w), q, qr, out, outr, nt);
+                  static_cast<const __half*>(w), q, qr, out, outr, nt, qcat);
 }
 
 cudaError_t launch_wvb_f16(const void* w, const float* x, Rows xr, float* out, Rows outr, int nt,

@@ -76,6 +76,22 @@ struct Rows {
     int64_t ts;   // token stride, floats
 };
 
+#ifdef __CUDACC__
+// M4B_FLAG_QCAT: out[t][h][ooff + c] = q[t][h][qoff + c] for the 64 rope values of head h (the
+// graph's concat of q_abs and q_pe), for the tokens t = k, k + nk, ... : the nk CTAs that serve
+// head h share its tokens, so each thread moves at most a few values (one L2 round trip).
+__device__ __forceinline__ void wkb_concat_rope(const float* __restrict__ q, Rows qr, int qoff,
+                                                float* __restrict__ out, Rows outr, int ooff,
+                                                int nt, int h, int k, int nk, int nthreads) {
+    const int count = k < nt ? (nt - k + nk - 1) / nk : 0;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < count * 64; i += nthreads) {
+        const int t = k + nk * (i >> 6), c = i & 63;
+        out[t * outr.ts + h * outr.hs + ooff + c] = q[t * qr.ts + h * qr.hs + qoff + c];
+    }
+}
+#endif
+
 // q_abs[t][h][r] = W_UK[h][r][:] . f16(q[t][h][:128]) for nt tokens; W_UK contiguous f16
 // [32][512][128], read once for all tokens.
 cudaError_t launch_wkb_f16(const void* w, const float* q, Rows qr, float* out, Rows outr, int nt,
@@ -118,6 +134,10 @@ struct KvWriteLaunch {
     float* kcur;                // [320] out (dst)
     float eps, freq_scale, ext_factor, attn_factor, theta_scale, corr0, corr1;
     uint32_t flags;
+    // slab != 0: kidx[0] is a row of the whole cache and kcache holds its rows [slab_base,
+    // slab_base + kcache_rows); a row held by another GPU's slab is skipped, not an error
+    int slab = 0;
+    int64_t slab_base = 0;
 };
 cudaError_t launch_kvwrite(const KvWriteLaunch& a, cudaStream_t stream);
 

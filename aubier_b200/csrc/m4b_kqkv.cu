@@ -771,16 +771,16 @@ __device__ __forceinline__ float butterfly_transpose_sum(float (&v)[N], int lane
 // first record, ss: the record stride in floats, s_ml: 2 * S floats of shared memory.  On return
 // every thread has mstar and l; threads tid < 128 have the unnormalised column sum o of column
 // d0 + tid.  Called by all CMB_THREADS threads.
-template <int R>
+template <int R, int RB = CWV_RB>
 __device__ __forceinline__ void merge_block_inflight(const float* __restrict__ ph, int S, size_t ss,
                                                      int d0, float* s_ml,
                                                      float (*s_red)[128], float* s_m, float* s_l,
                                                      float& mstar, float& l, float& o) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    float4 ov[CWV_RB];
+    float4 ov[RB];
     auto load_records = [&](int sb) {
 #pragma unroll
-        for (int k = 0; k < CWV_RB; ++k) {
+        for (int k = 0; k < RB; ++k) {
             const int s = sb + warp + 8 * k;
             ov[k] = s < S ? __ldg(reinterpret_cast<const float4*>(ph + s * ss + d0 + 4 * lane))
                           : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -818,7 +818,7 @@ __device__ __forceinline__ void merge_block_inflight(const float* __restrict__ p
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int sb = 0;;) {
 #pragma unroll
-        for (int k = 0; k < CWV_RB; ++k) {
+        for (int k = 0; k < RB; ++k) {
             const int s = sb + warp + 8 * k;
             if (s < S) {
                 const float a = s_ms[s];
@@ -828,7 +828,7 @@ __device__ __forceinline__ void merge_block_inflight(const float* __restrict__ p
                 acc.w = fmaf(a, ov[k].w, acc.w);
             }
         }
-        sb += 8 * CWV_RB;
+        sb += 8 * RB;
         if (sb >= S) break;
         load_records(sb);
     }
@@ -844,7 +844,7 @@ __device__ __forceinline__ void merge_block_inflight(const float* __restrict__ p
     }
 }
 
-template <int R>
+template <int R, int RB = CWV_RB>
 __device__ __forceinline__ void merge_head(const float* __restrict__ ph, int S, size_t ss,
                                            float* __restrict__ out, int record_out,
                                            float* s_ml) {
@@ -853,7 +853,7 @@ __device__ __forceinline__ void merge_head(const float* __restrict__ ph, int S, 
     const int d0 = blockIdx.y * 128;
     const int tid = threadIdx.x;
     float mstar, l, o;
-    merge_block_inflight<R>(ph, S, ss, d0, s_ml, s_red, s_m, s_l, mstar, l, o);
+    merge_block_inflight<R, RB>(ph, S, ss, d0, s_ml, s_red, s_m, s_l, mstar, l, o);
     if (tid < 128) {
         if (record_out) {
             out[d0 + tid] = o;
@@ -1003,7 +1003,8 @@ kqkv_ragged_combine_kernel(const float* __restrict__ part, const int32_t* __rest
         return;
     }
     const size_t ss = static_cast<size_t>(H) * (R + 4);
-    merge_head<R>(part + static_cast<size_t>(s_first + t) * ss + static_cast<size_t>(h) * (R + 4),
+    // a token's window spans a few CTAs' records: a shallow batch keeps registers (and occupancy)
+    merge_head<R, 4>(part + static_cast<size_t>(s_first + t) * ss + static_cast<size_t>(h) * (R + 4),
                   s_count, ss, orow, 0, s_ml);
 }
 

@@ -51,7 +51,7 @@ constexpr int WKB_R = 256;
 
 __global__ void __launch_bounds__(WKB_ROWS)
 wkb_q8_kernel(const uint8_t* __restrict__ w, const float* __restrict__ q, Rows qr,
-              float* __restrict__ out, Rows outr, int nt) {
+              float* __restrict__ out, Rows outr, int nt, int qcat) {
     __shared__ __align__(16) int8_t s_xq[kMaxSeqs][2][QK];
     __shared__ float s_xd[kMaxSeqs][2];
     const int h = blockIdx.x;
@@ -62,6 +62,7 @@ wkb_q8_kernel(const uint8_t* __restrict__ w, const float* __restrict__ q, Rows q
 #pragma unroll
     for (int i = 0; i < 17; ++i) wv[i] = __ldg(wr + i);
     pdl_wait();
+    if (qcat) wkb_concat_rope(q, qr, 2 * QK, out, outr, WKB_R, nt, h, blockIdx.y, gridDim.y, WKB_ROWS);
     // quantize (token, block) pairs: warp-wide amax, lane = element
     for (int pb = warp; pb < 2 * nt; pb += WKB_ROWS / 32) {
         const int t = pb >> 1, b = pb & 1;
@@ -209,12 +210,13 @@ __global__ void __launch_bounds__(KVW_ROW)
 kvwrite_tail_kernel(float* __restrict__ kcur, const float* __restrict__ nw,
                     __half* __restrict__ kcache, int64_t row_stride, int64_t n_rows,
                     const int64_t* __restrict__ kidx, const int32_t* __restrict__ posv,
-                    RopeArgs ra) {
+                    RopeArgs ra, int slab, int64_t slab_base) {
     __shared__ float s_red[KVW_ROW / 32];
     __shared__ float s_ss;
     const int tid = threadIdx.x;
     pdl_wait();
-    const int64_t row = kidx[0];
+    const int64_t grow = kidx[0];
+    const int64_t row = slab ? grow - slab_base : grow;   // row of this GPU's cache
     const int pos = posv[0];
     float v = 0.0f, ss = 0.0f;
     if (tid < KVW_LAT) {
@@ -259,7 +261,9 @@ kvwrite_tail_kernel(float* __restrict__ kcur, const float* __restrict__ nw,
     }
     __syncthreads();
     if (row < 0 || row >= n_rows) {
-        if (tid == 0) atomicExch(&g_status, DEV_STATUS_BADSEQ);
+        // one cache: a row outside it is an error; a slab: only a negative row is, any other row
+        // belongs to another GPU's slab
+        if (tid == 0 && (!slab || grow < 0)) atomicExch(&g_status, DEV_STATUS_BADSEQ);
         return;
     }
     kcache[row * row_stride + tid] = __float2half(kcur[tid]);
@@ -271,7 +275,8 @@ cudaError_t launch_wkb_q8(const void* w, const float* q, Rows qr, float* out, Ro
                           uint32_t flags, cudaStream_t stream) {
     using namespace q8;
     return launch(wkb_q8_kernel, dim3(kHeads, WKB_R / WKB_ROWS), dim3(WKB_ROWS), 0, stream, flags,
-                  static_cast<const uint8_t*>(w), q, qr, out, outr, nt);
+                  static_cast<const uint8_t*>(w), q, qr, out, outr, nt,
+                  (flags & M4B_FLAG_QCAT) ? 1 : 0);
 }
 
 cudaError_t launch_wvb_q8(const void* w, const float* x, Rows xr, float* out, Rows outr, int nt,
@@ -289,7 +294,7 @@ cudaError_t launch_kvwrite(const KvWriteLaunch& a, cudaStream_t stream) {
     RopeArgs ra = {a.eps, a.freq_scale, a.ext_factor, a.attn_factor, a.theta_scale, a.corr0, a.corr1};
     return launch(kvwrite_tail_kernel, dim3(1), dim3(KVW_ROW), 0, stream, a.flags | M4B_FLAG_PDL,
                   a.kcur, a.norm_w, static_cast<__half*>(a.kcache), a.kcache_row_stride,
-                  a.kcache_rows, a.kidx, a.pos, ra);
+                  a.kcache_rows, a.kidx, a.pos, ra, a.slab, a.slab_base);
 }
 
 }  // namespace m4b

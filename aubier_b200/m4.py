@@ -37,7 +37,7 @@ PART_STRIDE = LATENT + 4   # o[512], m (log2 units), l, 2 pad
 TILE_KEYS = 128            # keys per KQKV tile: splits are balanced over ceil(N / 128) tiles
 
 F32, F16, Q8_0, I32, I64 = 0, 1, 8, 26, 27
-FLAG_PDL, FLAG_KV_STATIC = 1, 2
+FLAG_PDL, FLAG_KV_STATIC, FLAG_QCAT = 1, 2, 4
 OK, EINVAL, ESCRATCH, ECUDA, EDEVICE, ENOTSUP, ETIMEOUT = range(7)
 
 OP_WKB, OP_KQKV, OP_PHASE = 0, 1, 2
@@ -86,6 +86,7 @@ def _load():
     for name in ("m4b_kqkv", "m4b_kqkv_partials"):
         getattr(lib, name).argtypes = [ctypes.POINTER(KqkvArgs), c_void_p]
     lib.m4b_phase.argtypes = [ctypes.POINTER(PhaseArgs), c_void_p]
+    lib.m4b_phase_kvwrite_slab.argtypes = [ctypes.POINTER(PhaseArgs), c_int64, c_void_p]
     lib.m4b_kqkv_ragged.argtypes = [ctypes.POINTER(RaggedArgs), c_void_p]
     lib.m4b_kqkv_ragged_scratch_bytes.argtypes = [c_int64]
     lib.m4b_kqkv_ragged_scratch_bytes.restype = c_uint64
@@ -415,12 +416,15 @@ MISTRAL_ROPE = {"freq_base": 10000.0, "freq_scale": 1.0 / 128.0, "ext_factor": 1
 def phase_kvwrite(cur: torch.Tensor, w_kva: torch.Tensor, norm_w: torch.Tensor,
                   kcache: torch.Tensor, kidx: torch.Tensor, pos: torch.Tensor,
                   rope: dict | None = None, out: torch.Tensor | None = None,
-                  flags: int = 0) -> torch.Tensor:
+                  flags: int = 0, slab_base: int | None = None) -> torch.Tensor:
     """GGML_OP_M4_PHASE selector 0, the KV-write (Mistral-Small-4 geometry): Kcur = norm(W_kva .
     cur) with YaRN rope on the last 64 values, written as f16 into kcache row kidx[0] (in place).
     cur f32 (4096,); w_kva Q8_0 bytes (320, 4352); norm_w f32 (256,); kcache f16 (N, 320);
     kidx int64 (1,) and pos int32 (1,) on the device; rope: the rope / norm scalars (default the
-    engine's, MISTRAL_ROPE).  Returns Kcur f32 (320,)."""
+    engine's, MISTRAL_ROPE).  Returns Kcur f32 (320,).
+    slab_base (additive, m4b_phase_kvwrite_slab): kcache is this GPU's slab of a sharded cache,
+    holding rows [slab_base, slab_base + N) of it, and kidx[0] indexes the whole cache: the row is
+    written only if this slab holds it."""
     _need_cuda("GGML_OP_M4_PHASE", cur, w_kva, norm_w, kcache, kidx, pos, out)
     rp = dict(MISTRAL_ROPE, **(rope or {}))
     if out is None:
@@ -440,7 +444,11 @@ def phase_kvwrite(cur: torch.Tensor, w_kva: torch.Tensor, norm_w: torch.Tensor,
     a.op_params[8] = int(rp["n_dims"])
     a.op_params[9] = int(rp["n_ctx_orig"])
     a.flags = flags
-    _check(_lib.m4b_phase(ctypes.byref(a), _stream()), "m4b_phase(0)")
+    if slab_base is None:
+        _check(_lib.m4b_phase(ctypes.byref(a), _stream()), "m4b_phase(0)")
+    else:
+        _check(_lib.m4b_phase_kvwrite_slab(ctypes.byref(a), c_int64(int(slab_base)), _stream()),
+               "m4b_phase_kvwrite_slab")
     return out
 
 

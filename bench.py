@@ -202,10 +202,10 @@ def run_reference(args, rank: int) -> None:
 # our arm: the two workloads
 # ---------------------------------------------------------------------------------------------
 class Workload:
-    """Per-rank device state of one workload: ``step(e2e)`` enqueues the L layer-steps (with
-    e2e=True it also moves the fresh query's rope half into Qcur), ``kq()`` the L launches of the
-    dominant kernel alone; ``q``/``out`` are the per-step input / output buffers the e2e timing
-    copies from / to the host."""
+    """Per-rank device state of one workload: ``step()`` enqueues the L layer-steps (WKB also
+    writes each query's rope half into Qcur, so the device-timed and the e2e graphs do the same
+    work), ``kq()`` the L launches of the dominant kernel alone; ``q``/``out`` are the per-step
+    input / output buffers the e2e timing copies from / to the host."""
 
     def close(self):
         pass
@@ -257,11 +257,10 @@ def slab_workload(args, rank, world, dev):
         dist.barrier()
     flags = m4.FLAG_PDL
 
-    def step(e2e: bool = False):
+    def step():
         for layer in range(L):
-            if e2e:   # the fresh query's rope half goes into Qcur as well
-                qcur[layer][:, R:].copy_(q[layer][:, NOPE:])
-            m4.wkb(wuk[layer], q[layer][:, :NOPE], out=qcur[layer][:, :R], flags=flags)
+            # WKB writes q_abs and (QCAT) the query's rope half: Qcur = concat(q_abs, q_pe)
+            m4.wkb(wuk[layer], q[layer][:, :NOPE], out=qcur[layer][:, :R], flags=flags | m4.FLAG_QCAT)
             m4.kqkv_partials(kc[layer], qcur[layer], None, SCALE, out=part,
                              flags=flags | m4.FLAG_KV_STATIC)
             if xchg is not None:   # one launch: merge, NVLink stores into every peer, wait, merge, W_UV
@@ -351,13 +350,12 @@ def mistral_workload(args, rank, world, dev):
     w.q, w.out = q, torch.empty(L, H, V, device=dev)
     flags = m4.FLAG_PDL   # no KV_STATIC: the KV-write two launches earlier writes the cache
 
-    def step(e2e: bool = False):
+    def step():
         for layer in range(L):
-            if e2e:
-                qcur[layer][:, RM:].copy_(q[layer][:, NOPEM:])
             m4.phase_kvwrite(cur[layer], wkv[layer], nw[layer], kc[layer], kidx, pos, out=kcur,
                              flags=flags)
-            m4.wkb(wuk[layer], q[layer][:, :NOPEM], out=qcur[layer][:, :RM], flags=flags)
+            m4.wkb(wuk[layer], q[layer][:, :NOPEM], out=qcur[layer][:, :RM],
+                   flags=flags | m4.FLAG_QCAT)
             m4.kqkv_partials(kc[layer], qcur[layer], None, scale, out=part, flags=flags)
             m4.phase_combine_wvb(wuv[layer], part, out=w.out[layer], attn_out=attn, flags=flags)
 
@@ -422,11 +420,10 @@ def ragged_workload(args, rank, world, dev):
     scratch = torch.empty(m4.kqkv_ragged_scratch_bytes(T), dtype=torch.uint8, device=dev)
     flags = m4.FLAG_PDL
 
-    def step(e2e: bool = False):
+    def step():
         for layer in range(L):
-            if e2e:
-                qcur[layer][:, :, R:].copy_(q[layer][:, :, NOPE:])
-            m4.wkb(wuk[layer], q[layer][:, :, :NOPE], out=qcur[layer][:, :, :R], flags=flags)
+            m4.wkb(wuk[layer], q[layer][:, :, :NOPE], out=qcur[layer][:, :, :R],
+                   flags=flags | m4.FLAG_QCAT)
             m4.kqkv_ragged(kc[layer], qcur[layer], base, length, SCALE, out=attn, scratch=scratch,
                            flags=flags | m4.FLAG_KV_STATIC)
             m4.phase_wvb(wuv[layer], attn, out=w.out[layer], flags=flags)
@@ -519,7 +516,7 @@ def run_ours(args, rank: int, world: int) -> None:
     out_host = torch.empty((args.steps,) + tuple(w.out.shape), pin_memory=True)
     graph_e2e = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph_e2e):
-        w.step(e2e=True)
+        w.step()
     graph_e2e.replay()
     torch.cuda.synchronize()
     barrier()

@@ -86,7 +86,12 @@ enum m4b_flags {
     M4B_FLAG_PDL       = 1u << 0,
     /* with M4B_FLAG_PDL: the KV cache is not written by the kernels immediately before this one,
        so KQKV may start streaming it before the preceding kernel finishes */
-    M4B_FLAG_KV_STATIC = 1u << 1
+    M4B_FLAG_KV_STATIC = 1u << 1,
+    /* m4b_wkb only (additive): also copy each query head's rope half -- the 64 floats that follow
+       q_nope in src1's head row -- into dst's head row right after the latent, so dst holds the
+       graph's Qcur = concat(q_abs, q_pe) (engine/m1_layer.cpp:443-447) without a separate copy.
+       Needs src1's head stride >= nope + 64 floats and dst's >= latent + 64 floats. */
+    M4B_FLAG_QCAT      = 1u << 2
 };
 
 /*
@@ -205,6 +210,18 @@ typedef struct m4b_phase_args {
 } m4b_phase_args;
 
 M4B_API int m4b_phase(const m4b_phase_args * args, m4b_stream_t stream);
+
+/*
+ * KV-append into a sharded cache (additive; the reference keeps the whole cache on one GPU,
+ * engine/m1_engine.cpp:2165): PHASE selector 0 (args as m4b_phase, op_params[0] = 0) for a cache
+ * split into contiguous slabs of rows, one per GPU.  kidx[0] is the new row's index in the WHOLE
+ * cache; src[3] is this GPU's slab, which holds rows [slab_base, slab_base + src[3].ne[1]).  Every
+ * GPU computes Kcur (dst); only the GPU whose slab holds the row writes it.  A row held by another
+ * slab is skipped without error; a negative kidx sets M4B_EINVAL in m4b_device_status, as
+ * selector 0 does for a row outside its cache.  slab_base < 0 is refused (M4B_EINVAL).
+ */
+M4B_API int m4b_phase_kvwrite_slab(const m4b_phase_args * args, int64_t slab_base,
+                                   m4b_stream_t stream);
 
 /*
  * The KV-slab exchange between the GPUs of one node, fused into the merge kernels (no counterpart

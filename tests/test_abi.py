@@ -164,6 +164,10 @@ def test_entry_points_refuse_bad_operands_before_any_cuda_call():
     kv = m4.PhaseArgs()                      # a KV-write over a BASELINE-row cache: no such op
     kv.src[3] = KC
     assert _call(lib.m4b_phase, kv) == m4.ENOTSUP
+    assert lib.m4b_phase_kvwrite_slab(None, 0, None) == m4.EINVAL
+    assert lib.m4b_phase_kvwrite_slab(ctypes.byref(kv), -1, None) == m4.EINVAL
+    p.op_params[0] = 1                       # the slab entry is the KV-write only
+    assert lib.m4b_phase_kvwrite_slab(ctypes.byref(p), 0, None) == m4.EINVAL
     assert lib.m4b_kqkv(None, None) == m4.EINVAL
 
 

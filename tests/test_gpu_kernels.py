@@ -65,6 +65,26 @@ def test_wkb_writes_into_qcur_view(m4):
     assert np.array_equal(got[:, G.R:], q[:, G.nope:])
 
 
+@pytest.mark.parametrize("nt", [1, 3])
+def test_wkb_qcat_writes_the_rope_half(m4, nt):
+    """M4B_FLAG_QCAT: WKB also copies each head's 64 rope values behind the latent, so dst holds
+    Qcur = concat(q_abs, q_pe); q_abs is bit-identical to a call without the flag."""
+    _, w_uk, _, _ = make_layer(71, 1)
+    q = normal(72, nt * G.H * G.dq).astype(np.float32).reshape(nt, G.H, G.dq)
+    qd, wk = dev(q), dev(w_uk)
+    plain = host(m4.wkb(wk, qd[:, :, :G.nope]))
+    qcur = torch.full((nt, G.H, G.D), 7.0, device="cuda")
+    m4.wkb(wk, qd[:, :, :G.nope], out=qcur[:, :, :G.R], flags=m4.FLAG_QCAT)
+    got = host(qcur)
+    assert np.array_equal(got[:, :, :G.R], plain)
+    assert np.array_equal(got[:, :, G.R:], q[:, :, G.nope:])
+    with pytest.raises(m4.M4Error):   # no room behind the latent in dst
+        m4.wkb(wk, qd[:, :, :G.nope], out=torch.empty(nt, G.H, G.R, device="cuda"),
+               flags=m4.FLAG_QCAT)
+    with pytest.raises(m4.M4Error):   # no rope values behind q_nope in src1
+        m4.wkb(wk, qd[:, :, :G.nope].contiguous(), out=qcur[:, :, :G.R], flags=m4.FLAG_QCAT)
+
+
 # ------------------------------------------------------------------------------------- KQKV
 @pytest.mark.parametrize("N", [1, 7, 127, 128, 129, 255, 256, 257, 640, 1000, 4096])
 def test_kqkv_matches_oracle(m4, N):

@@ -152,6 +152,18 @@ def test_layer_step_matches_reference_golden(m4, name):
     assert rel_to_max(out, gold["out"]) <= Q8_CHAIN_TOL
 
 
+def test_wkb_q8_qcat_writes_the_rope_half(m4):
+    """M4B_FLAG_QCAT at the Mistral geometry: q (32, 128) = nope 64 + rope 64; Qcur (32, 320)."""
+    q, w_uk, _, _ = make_layer_q8(73, 1)
+    qd, wk = dev(q), dev(w_uk)
+    plain = host(m4.wkb(wk, qd[:, :G.nope]))
+    qcur = torch.full((G.H, G.D), 7.0, device="cuda")
+    m4.wkb(wk, qd[:, :G.nope], out=qcur[:, :G.R], flags=m4.FLAG_QCAT)
+    got = host(qcur)
+    assert np.array_equal(got[:, :G.R], plain)
+    assert np.array_equal(got[:, G.R:], q[:, G.nope:])
+
+
 # ------------------------------------------------------------------------------------- KV-write
 def _kvwrite_gpu(m4, cur, w, nw, kc, kidx, pos, rope=None):
     kcd = dev(kc)
@@ -194,6 +206,39 @@ def test_kvwrite_row_outside_cache_writes_nothing(m4):
     assert np.array_equal(cache, kc)
     ref = O.kvwrite(cur, w, nw, None, 0, 5, MISTRAL_ROPE, O.FUSED)
     assert rel_to_max(kcur, ref) <= 1e-5                                # Kcur is still produced
+    assert m4.device_status() == m4.OK
+
+
+@pytest.mark.parametrize("kidx", [0, 9, 23, 39])
+def test_kvwrite_into_sharded_slabs_equals_one_cache(m4, kidx):
+    """m4b_phase_kvwrite_slab: a 40-row cache split into slabs of 16 / 16 / 8 rows (one per GPU in
+    a sharded deployment, emulated here on one GPU).  Every slab computes the same Kcur as the
+    one-cache KV-write; only the slab holding global row kidx writes it, at kidx - slab_base, and
+    the others are untouched and report no error."""
+    cur, w, nw, kc = make_kvwrite(62, 40)
+    kcur_ref, cache_ref = _kvwrite_gpu(m4, cur, w, nw, kc, kidx, 77)
+    assert m4.device_status() == m4.OK
+    idx, pos = dev(np.array([kidx], np.int64)), dev(np.array([77], np.int32))
+    args = [dev(cur), dev(w), dev(nw)]
+    slabs = [(0, 16), (16, 32), (32, 40)]
+    for base, end in slabs:
+        part = dev(kc[base:end])
+        kcur = host(m4.phase_kvwrite(*args, part, idx, pos, slab_base=base))
+        assert np.array_equal(kcur, kcur_ref)
+        assert np.array_equal(host(part), cache_ref[base:end])           # own row written, no other
+        assert m4.device_status() == m4.OK
+
+
+def test_kvwrite_slab_refusals(m4):
+    cur, w, nw, kc = make_kvwrite(63, 8)
+    args = [dev(cur), dev(w), dev(nw), dev(kc)]
+    pos = dev(np.array([1], np.int32))
+    with pytest.raises(m4.M4Error):
+        m4.phase_kvwrite(*args, dev(np.array([0], np.int64)), pos, slab_base=-1)
+    part = args[3]
+    m4.phase_kvwrite(*args[:3], part, dev(np.array([-3], np.int64)), pos, slab_base=8)
+    assert m4.device_status() == m4.EINVAL                              # a negative row is an error
+    assert np.array_equal(host(part), kc)
     assert m4.device_status() == m4.OK
 
 
