@@ -171,6 +171,22 @@ def test_entry_points_refuse_bad_operands_before_any_cuda_call():
     assert lib.m4b_kqkv(None, None) == m4.EINVAL
 
 
+def test_wkb_qcat_needs_room_for_the_rope_half():
+    """M4B_FLAG_QCAT copies 64 rope values behind q_nope into dst behind the latent: both head rows
+    must be long enough, checked before any CUDA call (without a GPU a valid call then fails on the
+    device check, not on the arguments)."""
+    lib = m4.lib()
+    w = m4.WkbArgs()
+    w.src0, w.flags = WUK, m4.FLAG_QCAT
+    w.src1, w.dst = QNOPE, QABS                      # dst head stride 512 floats: no room
+    assert _call(lib.m4b_wkb, w) == m4.EINVAL
+    w.src1 = contiguous(m4.F32, [128, 32, 1, 1], 4)   # q_nope alone: no rope values behind it
+    w.dst = T(m4.F32, [512, 32, 1, 1], [4, 2304, 2304 * 32, 2304 * 32])
+    assert _call(lib.m4b_wkb, w) == m4.EINVAL
+    w.src1 = QNOPE                                    # head rows of 192 and 576 floats: accepted
+    assert _call(lib.m4b_wkb, w) != m4.EINVAL
+
+
 def test_exchange_refuses_bad_arguments_before_any_cuda_call():
     from aubier_b200 import exchange  # noqa: F401  (declares the argument types)
     lib = m4.lib()
