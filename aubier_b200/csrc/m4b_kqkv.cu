@@ -706,7 +706,13 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
             if (lane == 0) mbar_arrive(&C.p_full[i & 1]);
             if (seg_end && g + 1 < nseg) {
                 // a segment other than the last ends here: write its record once MMA2(i) is
-                // done (the next segment's MMA2 waits for P(i+1), written after this)
+                // done (the next segment's MMA2 waits for P(i+1), written after this).  o_done
+                // completes one phase per MMA2, and a parity wait cannot tell phase i from phase
+                // i - 2.  Here phases up to i - 2 are complete (MMA2(i-2) was issued before
+                // MMA1(i), whose S this thread has read), but MMA2(i-1) may still run: wait for
+                // phase i - 1 first, so that the wait for phase i is not answered by phase i - 2.
+                ok = warp_wait(&C.o_done, (i - 1) & 1, abort_flag);
+                if (!ok) break;
                 flush(sg, &C.o_done, i & 1);
                 if (!ok) break;
 #pragma unroll

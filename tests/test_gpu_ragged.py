@@ -155,6 +155,15 @@ def test_ragged_many_windows_per_cta(m4):
     _ragged_vs_oracle(m4, 74, lengths, bases, int(sum(lengths)))
 
 
+def test_ragged_short_first_segments(m4):
+    # 64 windows of 11-14 tiles over 148 SMs (~5.5 tiles per CTA): 10 or 11 CTAs each start with
+    # the last 1, 2, 3 or 4 tiles of one window and then go on to the next.  A segment that ends
+    # after 1-2 tiles reads its accumulator while the matrix unit may still be two tiles behind.
+    lengths = [1400 + (i * 97) % 300 for i in range(64)]
+    bases = packed_bases(lengths)
+    _ragged_vs_oracle(m4, 80, lengths, bases, int(sum(lengths)))
+
+
 def test_ragged_one_window_equals_single_token_op(m4):
     N = 20000
     kc = dev(cache(75, N))
