@@ -272,18 +272,19 @@ int check_kvwrite(const m4b_phase_args& a) {
     if (!type_ne(w, M4B_TYPE_Q8_0, kKvwIn, 320, 1, 1) || w.nb[0] != kQ8Block ||
         w.nb[1] != static_cast<uint64_t>(kKvwIn / 32) * kQ8Block || !w.data || !aligned(w.data, 2))
         return M4B_EINVAL;
+    // the tail moves value pairs: norm_w and Kcur 8-byte aligned, cache rows 4-byte aligned
     if (!type_ne(nw, M4B_TYPE_F32, 256, 1, 1, 1) || nw.nb[0] != 4 || !nw.data ||
-        !aligned(nw.data, 4))
+        !aligned(nw.data, 8))
         return M4B_EINVAL;
     if (kc.type != M4B_TYPE_F16 || kc.ne[0] != 320 || kc.ne[1] < 1 || kc.ne[2] != 1 ||
-        kc.ne[3] != 1 || kc.nb[0] != 2 || kc.nb[1] % 2 != 0 || kc.nb[1] < 640 || !kc.data ||
-        !aligned(kc.data, 2))
+        kc.ne[3] != 1 || kc.nb[0] != 2 || kc.nb[1] % 4 != 0 || kc.nb[1] < 640 || !kc.data ||
+        !aligned(kc.data, 4))
         return M4B_EINVAL;
     if (!type_ne(kidx, M4B_TYPE_I64, 1, 1, 1, 1) || !kidx.data || !aligned(kidx.data, 8))
         return M4B_EINVAL;
     if (!type_ne(pos, M4B_TYPE_I32, 1, 1, 1, 1) || !pos.data || !aligned(pos.data, 4))
         return M4B_EINVAL;
-    if (!type_ne(d, M4B_TYPE_F32, 320, 1, 1, 1) || d.nb[0] != 4 || !d.data || !aligned(d.data, 4))
+    if (!type_ne(d, M4B_TYPE_F32, 320, 1, 1, 1) || d.nb[0] != 4 || !d.data || !aligned(d.data, 8))
         return M4B_EINVAL;
     if (a.op_params[8] != 64) return M4B_EINVAL;   // n_dims (m4-phase.cu:256)
     return M4B_OK;
@@ -645,6 +646,12 @@ int m4b_last_cuda_error(const char** name) {
     const int e = last_cuda_error().exchange(0);
     if (name) *name = cudaGetErrorName(static_cast<cudaError_t>(e));
     return e;
+}
+
+int m4b_set_wait_limit_cycles(int64_t cycles) {
+    const long long v = cycles > 0 ? static_cast<long long>(cycles) : M4B_WAIT_LIMIT_CYCLES;
+    if (note(cudaMemcpyToSymbol(g_wait_limit, &v, sizeof(v))) != cudaSuccess) return M4B_ECUDA;
+    return note(cudaDeviceSynchronize()) == cudaSuccess ? M4B_OK : M4B_ECUDA;
 }
 
 int m4b_device_status(m4b_stream_t stream) {

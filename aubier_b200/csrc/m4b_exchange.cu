@@ -69,14 +69,14 @@ __device__ __forceinline__ void st_word(uint64_t* a, float v, uint32_t e) {
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(w) : "memory");
 }
 
-// Poll one word until it carries epoch e; bounded: after M4B_WAIT_LIMIT_CYCLES (counted from t0)
+// Poll one word until it carries epoch e; bounded: after g_wait_limit cycles (counted from t0)
 // the device status becomes TIMEOUT and whatever the word holds is returned.
 __device__ __forceinline__ float ld_word(const uint64_t* a, uint32_t e, long long t0) {
     uint64_t w;
     for (;;) {
         asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(a) : "memory");
         if (static_cast<uint32_t>(w >> 32) == e) break;
-        if (clock64() - t0 > M4B_WAIT_LIMIT_CYCLES) {
+        if (wait_expired(t0)) {
             atomicExch(&g_status, DEV_STATUS_TIMEOUT);
             break;
         }
@@ -417,6 +417,31 @@ M4B_API int m4b_exchange_open(m4b_exchange* x, const void* handles) {
             return M4B_ECUDA;
         x->peer[r] = static_cast<char*>(p);
         x->opened[r] = true;
+    }
+    return M4B_OK;
+}
+
+M4B_API int m4b_exchange_open_local(m4b_exchange* x, m4b_exchange* const* all, int n) {
+    if (!x || !all || n != x->world || all[x->rank] != x) return M4B_EINVAL;
+    for (int r = 0; r < n; ++r)
+        if (!all[r] || all[r]->world != x->world || all[r]->rank != r || !all[r]->local)
+            return M4B_EINVAL;
+    for (int r = 0; r < n; ++r) {
+        if (r == x->rank || x->opened[r]) continue;
+        if (all[r]->device != x->device) {   // another GPU of this process: direct peer access
+            int can = 0;
+            if (cudaDeviceCanAccessPeer(&can, x->device, all[r]->device) != cudaSuccess)
+                return M4B_ECUDA;
+            if (!can) return M4B_EDEVICE;
+            int cur = 0;
+            if (cudaGetDevice(&cur) != cudaSuccess || cudaSetDevice(x->device) != cudaSuccess)
+                return M4B_ECUDA;
+            const cudaError_t e = cudaDeviceEnablePeerAccess(all[r]->device, 0);
+            if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();   // clear it
+            cudaSetDevice(cur);
+            if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) return M4B_ECUDA;
+        }
+        x->peer[r] = all[r]->local;   // same process: the pointer itself, nothing to unmap
     }
     return M4B_OK;
 }

@@ -12,6 +12,11 @@
 // array's name as a device address (in host code it names a host-side stand-in), so the first
 // call on a device -- with that device current -- asks the runtime for the real address with
 // cudaGetSymbolAddress and caches it per device; make that first call before any stream capture.
+// The cache lives as long as the process's primary context on that device: after a
+// cudaDeviceReset the library image, and with it the array, is loaded again, possibly elsewhere,
+// so a process that resets a device must not call this entry point on it afterwards.  Concurrent
+// first calls from several host threads all store the same address (the cache entries are
+// atomic, so this is well defined).
 // All calls on a device share the array and it keeps whatever the last call wrote: every split
 // writes its whole record before the merge reads it, so nothing needs clearing, but two calls
 // whose kernels overlap on the GPU (two streams, no ordering between them) race on the records.
@@ -25,7 +30,8 @@ constexpr int kStaticRecords = kMaxSplits * kHeads;   // 148 splits x 32 heads, 
 
 static __device__ __align__(256) float g_kqkv_static_part[kStaticRecords * kPartStride];
 
-float* g_addr[64] = {};   // cached device address of the array, per device ordinal
+// cached device address of the array, per device ordinal (nullptr until the first call there)
+std::atomic<float*> g_addr[64] = {};
 
 }  // namespace noalloc
 }  // namespace m4b
@@ -43,14 +49,17 @@ extern "C" M4B_API int m4b_kqkv_static_scratch(const m4b_kqkv_args* a, m4b_strea
     if (static_cast<int64_t>(splits) * kHeads > noalloc::kStaticRecords)
         return M4B_ESCRATCH;   // more split records than the static array holds
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return M4B_ECUDA;
-    if (noalloc::g_addr[dev] == nullptr) {
+    if (note(cudaGetDevice(&dev)) != cudaSuccess) return M4B_ECUDA;
+    if (dev < 0 || dev >= 64) return M4B_EDEVICE;
+    float* part = noalloc::g_addr[dev].load(std::memory_order_acquire);
+    if (part == nullptr) {
         void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, noalloc::g_kqkv_static_part) != cudaSuccess || p == nullptr)
+        if (note(cudaGetSymbolAddress(&p, noalloc::g_kqkv_static_part)) != cudaSuccess ||
+            p == nullptr)
             return M4B_ECUDA;
-        noalloc::g_addr[dev] = static_cast<float*>(p);
+        part = static_cast<float*>(p);
+        noalloc::g_addr[dev].store(part, std::memory_order_release);
     }
-    float* part = noalloc::g_addr[dev];
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     cudaError_t e = launch_kqkv_partials(make_kqkv_launch(*a, geom, splits, part), s);
     if (e != cudaSuccess) return M4B_ECUDA;

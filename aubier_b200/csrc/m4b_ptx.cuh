@@ -1,6 +1,6 @@
 // m4b_ptx.cuh -- thin inline-PTX wrappers for the sm_100a features the M4 kernels use:
 // mbarriers (with bounded waits), TMA tile loads, tcgen05 MMA / TMEM, programmatic dependent
-// launch.  Every wait here is bounded: after M4B_WAIT_LIMIT_CYCLES the wait gives up, sets the
+// launch.  Every wait here is bounded: after g_wait_limit cycles the wait gives up, sets the
 // CTA's abort flag and the device status word, and returns false, so a kernel never spins forever.
 #pragma once
 
@@ -11,6 +11,9 @@
 #ifndef M4B_WAIT_LIMIT_CYCLES
 #define M4B_WAIT_LIMIT_CYCLES (1ll << 31)   // ~1 s at 2 GHz
 #endif
+// Waits shorter than this never read the settable limit below, so the limit's global load stays
+// off the fast path (a wait that lasts 2^20 cycles, ~0.5 ms, is already far off it).
+#define M4B_WAIT_LIMIT_MIN_CYCLES (1ll << 20)
 
 namespace m4b {
 
@@ -18,6 +21,16 @@ namespace m4b {
 // m4b_device_status(); a kernel that hits it returns early and leaves its outputs undefined.
 // Defined here: the library is one translation unit (m4b_lib.cu).
 __device__ unsigned int g_status = 0;
+
+// The wait limit in SM cycles, per device; m4b_set_wait_limit_cycles changes it (a test shortens
+// it to make a wait run out in milliseconds).  Values below M4B_WAIT_LIMIT_MIN_CYCLES act as that.
+__device__ long long g_wait_limit = M4B_WAIT_LIMIT_CYCLES;
+
+// True once a wait that began at t0 has lasted past the limit.
+__device__ __forceinline__ bool wait_expired(long long t0) {
+    const long long dt = clock64() - t0;
+    return dt > M4B_WAIT_LIMIT_MIN_CYCLES && dt > *static_cast<volatile long long*>(&g_wait_limit);
+}
 
 // DEV_STATUS_BADSEQ: a ragged window outside the cache (the window was treated as empty).
 enum : unsigned int { DEV_STATUS_OK = 0, DEV_STATUS_TIMEOUT = 1, DEV_STATUS_BADSEQ = 2 };
@@ -84,7 +97,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     while (true) {
         if (mbar_try_wait(addr, parity)) return true;
         if (*abort_flag) return false;
-        if (clock64() - t0 > M4B_WAIT_LIMIT_CYCLES) {
+        if (wait_expired(t0)) {
             *abort_flag = 1;
             atomicExch(&g_status, DEV_STATUS_TIMEOUT);
             return false;
@@ -98,7 +111,7 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
     const uint32_t addr = smem_u32(bar);
     const long long t0 = clock64();
     while (!mbar_try_wait(addr, parity)) {
-        if (clock64() - t0 > M4B_WAIT_LIMIT_CYCLES) break;
+        if (wait_expired(t0)) break;
     }
 }
 

@@ -25,6 +25,8 @@ _lib = m4.lib()
 _lib.m4b_exchange_create.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]
 _lib.m4b_exchange_ipc_handle.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
 _lib.m4b_exchange_open.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+_lib.m4b_exchange_open_local.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p),
+                                         ctypes.c_int]
 _lib.m4b_exchange_detach.argtypes = [ctypes.c_void_p]
 _lib.m4b_exchange_destroy.argtypes = [ctypes.c_void_p]
 _lib.m4b_exchange_publish.argtypes = [ctypes.c_void_p, ctypes.POINTER(m4.PhaseArgs), ctypes.c_void_p]

@@ -99,6 +99,7 @@ def _load():
                                     ctypes.POINTER(c_int32)]
     lib.m4b_resolve_flag.argtypes = [c_int, c_int, c_int, c_int, ctypes.POINTER(c_int)]
     lib.m4b_device_status.argtypes = [c_void_p]
+    lib.m4b_set_wait_limit_cycles.argtypes = [c_int64]
     lib.m4b_last_cuda_error.argtypes = [ctypes.POINTER(ctypes.c_char_p)]
     lib.m4b_strerror.argtypes = [c_int]
     lib.m4b_strerror.restype = ctypes.c_char_p
@@ -475,3 +476,9 @@ def resolve_flag(flag: int, gpu_core: bool, nt: int = 1, ragged_ok: bool = False
 def device_status() -> int:
     """Synchronise the current stream and return (and clear) the device status word."""
     return int(_lib.m4b_device_status(_stream()))
+
+
+def set_wait_limit_cycles(cycles: int) -> None:
+    """How long the kernels' bounded waits last before giving up, in SM cycles, on the current
+    device (<= 0 restores the default, about 1 s).  Synchronises the device: not capturable."""
+    _check(_lib.m4b_set_wait_limit_cycles(c_int64(int(cycles))), "m4b_set_wait_limit_cycles")

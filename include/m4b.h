@@ -184,7 +184,13 @@ M4B_API int m4b_kqkv_static_scratch(const m4b_kqkv_args * args, m4b_stream_t str
  * GGML_OP_M4_PHASE -- the remaining per-token phases, selected by op_params[0].
  * Replaces ggml_cuda_m4_phase (patches/ggml-m4/m4-phase.cu:205-277); builders
  * ggml_m4_phase_kvwrite / ggml_m4_phase_wvb (ggml.c:3461-3539).
- *   phase 0  KV-write   (MISTRAL_SMALL geometry)                          -> M4B_ENOTSUP here
+ *   phase 0  KV-write   (MISTRAL_SMALL geometry, the reference's selector 0, m4-phase.cu:97-200):
+ *                       src0 cur F32 [4096]; src1 W_kva Q8_0 [4096, 320]; src2 kv norm weight
+ *                       F32 [256]; src3 kcache F16 [320, N] (written in place at row kidx[0]);
+ *                       src4 kidx I64 [1]; src5 pos I32 [1] (both read on the device only);
+ *                       dst Kcur F32 [320].  Kcur and the norm weight 8-byte aligned, cache
+ *                       rows 4-byte aligned.  A row outside the cache writes nothing and makes
+ *                       m4b_device_status() report M4B_EINVAL.  BASELINE has no W_kva: M4B_ENOTSUP
  *   phase 1  WVB        src0 W_UV F16 [512, 128, 32]; src1 x F32 [512, T, 32] (nb[2] head
  *                       stride); dst F32 [128, T, 32].  T = 1 in the reference's op; additively
  *                       1 <= T <= 64 tokens (token stride nb[1]) share one read of W_UV
@@ -238,8 +244,9 @@ M4B_API int m4b_phase_kvwrite_slab(const m4b_phase_args * args, int64_t slab_bas
  * exchange the M4B_IPC_HANDLE_BYTES handles of all ranks (m4b_exchange_ipc_handle) through any
  * host channel, then m4b_exchange_open with all of them, rank-ordered.  The two launch entry
  * points are plain launches (capturable); every GPU must call them the same number of times.
- * A peer that never publishes makes the combine give up after ~1 s and report M4B_ETIMEOUT through
- * m4b_device_status(); the output of that call is undefined.
+ * A peer that never publishes makes the combine give up after the wait limit (~1 s by default,
+ * m4b_set_wait_limit_cycles) and report M4B_ETIMEOUT through m4b_device_status(); the output of
+ * that call is undefined.
  * Tear-down: every rank calls m4b_exchange_detach (unmaps the peers' buffers), then all ranks meet
  * on the host, then each calls m4b_exchange_destroy (frees its own buffer) -- an exporting process
  * must not free a buffer that another process still has mapped.
@@ -250,6 +257,13 @@ typedef struct m4b_exchange m4b_exchange;
 M4B_API int m4b_exchange_create(int world, int rank, m4b_exchange ** out);
 M4B_API int m4b_exchange_ipc_handle(const m4b_exchange * x, void * handle_out);
 M4B_API int m4b_exchange_open(m4b_exchange * x, const void * handles);
+/* Set-up when every rank's exchange lives in this one process (one host thread or process driving
+ * several GPUs, as ggml-cuda's multi-GPU backend does): all[r] is rank r's exchange, created here
+ * on its own device, n == world.  The peers' buffers are used through their own pointers (peer
+ * access between the devices is enabled; no IPC mapping), so tear-down needs no meeting: destroy
+ * the exchanges once no launch uses them.  Kernels of different ranks that wait on each other
+ * must run on different GPUs; on one GPU, run every rank's publish before any rank's combine. */
+M4B_API int m4b_exchange_open_local(m4b_exchange * x, m4b_exchange * const * all, int n);
 M4B_API int m4b_exchange_detach(m4b_exchange * x);
 M4B_API int m4b_exchange_destroy(m4b_exchange * x);
 M4B_API int m4b_exchange_publish(m4b_exchange * x, const m4b_phase_args * args, m4b_stream_t stream);
@@ -287,6 +301,16 @@ M4B_API int m4b_resolve_flag(int flag, int gpu_core, int nt, int ragged_ok, int 
 /* Reads and clears the device status word; synchronises the stream.  M4B_OK, M4B_ETIMEOUT (a
    bounded wait gave up) or M4B_EINVAL (a ragged window outside the cache). */
 M4B_API int m4b_device_status(m4b_stream_t stream);
+
+/*
+ * Sets how long every bounded wait of the kernels lasts before it gives up (SM clock cycles; the
+ * default, also restored by cycles <= 0, is 2^31, about 1 s).  No counterpart in the reference,
+ * whose kernels never wait on another agent.  Limits below 2^20 cycles act as 2^20.  Applies to
+ * the current device; synchronises it, so call it outside stream capture and with no kernel of
+ * this library in flight.  A test shortens the limit to make a wait that nothing will end (an
+ * exchange whose peer never publishes) run out in milliseconds.
+ */
+M4B_API int m4b_set_wait_limit_cycles(int64_t cycles);
 
 /* The last CUDA runtime error (a cudaError_t value; 0 = none) behind an M4B_ECUDA from a launch
    entry point, with its name in *name when name is not NULL.  Reading clears it. */

@@ -171,6 +171,32 @@ def test_entry_points_refuse_bad_operands_before_any_cuda_call():
     assert lib.m4b_kqkv(None, None) == m4.EINVAL
 
 
+def test_static_scratch_entry_refuses_bad_operands_before_any_cuda_call():
+    """m4b_kqkv_static_scratch validates like m4b_kqkv before it touches the runtime (no device
+    check, no symbol lookup, no launch)."""
+    lib = m4.lib()
+    fn = lib.m4b_kqkv_static_scratch
+    fn.argtypes = [ctypes.POINTER(m4.KqkvArgs), ctypes.c_void_p]
+    assert lib.m4b_kqkv_static_scratch(None, None) == m4.EINVAL
+    a = m4.KqkvArgs()
+    a.src0, a.src1, a.src2, a.dst = KC, QCUR, MASK, ATTN
+    a.kq_scale = 0.07
+    a.dst = T(m4.F32, [256, 1, 32, 1], [4, 1024, 1024, 1024 * 32])   # latent 256 vs a 576 row
+    assert _call(fn, a) == m4.EINVAL
+    a.dst = ATTN
+    a.src2 = contiguous(m4.F32, [N - 1, 1, 1, 1], 4)                 # mask shorter than n_kv
+    assert _call(fn, a) == m4.EINVAL
+    a.src2 = MASK
+    a.src0 = contiguous(m4.F32, [576, N, 1, 1], 4)                   # f32 cache
+    assert _call(fn, a) == m4.EINVAL
+    a.src0 = KC
+    a.kq_scale = float("nan")
+    assert _call(fn, a) == m4.EINVAL
+    a.kq_scale = 0.07
+    a.dst = T(m4.F32, [512, 1, 32, 1], [4, 2048, 2048, 2048 * 32], addr=0)   # no output
+    assert _call(fn, a) == m4.EINVAL
+
+
 def test_wkb_qcat_needs_room_for_the_rope_half():
     """M4B_FLAG_QCAT copies 64 rope values behind q_nope into dst behind the latent: both head rows
     must be long enough, checked before any CUDA call (without a GPU a valid call then fails on the
@@ -198,6 +224,7 @@ def test_exchange_refuses_bad_arguments_before_any_cuda_call():
     assert lib.m4b_exchange_destroy(None) == m4.OK
     assert lib.m4b_exchange_ipc_handle(None, None) == m4.EINVAL
     assert lib.m4b_exchange_open(None, None) == m4.EINVAL
+    assert lib.m4b_exchange_open_local(None, None, 0) == m4.EINVAL
     p = m4.PhaseArgs()
     assert lib.m4b_exchange_publish(None, ctypes.byref(p), None) == m4.EINVAL
     assert lib.m4b_exchange_combine_wvb(None, ctypes.byref(p), None) == m4.EINVAL
