@@ -197,76 +197,82 @@ kvwrite_gemv_kernel(const float* __restrict__ cur, const uint8_t* __restrict__ w
     if (tid == 0) kcur[o] = s_part[0] + s_part[1] + s_part[2] + s_part[3];
 }
 
-// tail: one CTA of 320 threads (thread i owns Kcur[i]).  RMS norm of [0, 256): warp butterflies,
-// then the 10 warp partials summed in order by thread 0 (m4-phase.cu:153-164); rope of [256, 320)
-// in NORMAL mode (pairs (2p, 2p+1)), YaRN (rope_yarn of ggml, angle pos * theta_scale^p as
-// m4-phase.cu:171-190); then Kcur and its f16 image in cache row kidx[0].  kidx and pos are read
-// on the device.  A cache row outside [0, n_rows) writes nothing and sets the device status.
+// ---- KV-write tail: finishes the 320 pre-norm values the gemv left in Kcur.
+//   Kcur[0, 256)   = kv[0, 256) / sqrt(mean(kv[0, 256)^2) + eps) * norm_w      (ggml rms_norm, mul)
+//   Kcur[256, 320) = the 32 pairs (kv[256 + 2p], kv[257 + 2p]) rotated by the YaRN angle of pair p
+//                    at position pos (ggml rope, NORMAL mode, ggml-cpu/ops.cpp:6179-6201)
+// then f16(Kcur) into cache row kidx[0].  One CTA of 5 warps; thread t owns the value pair
+// (2t, 2t + 1): warps 0-3 the 128 latent pairs, warp 4 the 32 rope pairs, so every load and store
+// moves a float2 (a half2 into the cache).  The sum of squares is reduced per warp by shuffles;
+// each thread then adds the 4 warp totals itself, in warp order, so the scale needs no second
+// barrier.  kidx and pos are read on the device; a cache row outside [0, n_rows) is not written
+// and sets the device status.
 struct RopeArgs {
     float eps, freq_scale, ext_factor, attn_factor, theta_scale, corr0, corr1;
 };
 
-__global__ void __launch_bounds__(KVW_ROW)
+constexpr int KVT_LAT_PAIRS = KVW_LAT / 2;           // 128: warps 0-3
+constexpr int KVT_ROPE_PAIRS = KVW_ROPE / 2;         // 32: warp 4
+constexpr int KVT_THREADS = KVT_LAT_PAIRS + KVT_ROPE_PAIRS;
+
+// ggml's YaRN blend for pair p: 1 below corr0, 0 above corr1, linear between
+// (rope_yarn_ramp, evaluated at i0 / 2 = p).
+__device__ __forceinline__ float yarn_ramp(float corr_lo, float corr_hi, int p) {
+    const float t = (static_cast<float>(p) - corr_lo) / fmaxf(0.001f, corr_hi - corr_lo);
+    return 1.0f - fminf(1.0f, fmaxf(0.0f, t));
+}
+
+// The rotation (cos, sin), magnitude included, of pair p at position pos (ggml rope_yarn).
+__device__ __forceinline__ float2 yarn_rotation(const RopeArgs& ra, int pos, int p) {
+    const float ang_extrap = static_cast<float>(pos) * powf(ra.theta_scale, static_cast<float>(p));
+    const float ang_interp = ra.freq_scale * ang_extrap;
+    float ang = ang_interp, mag = ra.attn_factor;
+    if (ra.ext_factor != 0.0f) {
+        const float blend = yarn_ramp(ra.corr0, ra.corr1, p) * ra.ext_factor;
+        ang = ang_interp * (1.0f - blend) + ang_extrap * blend;
+        mag *= 1.0f + 0.1f * logf(1.0f / ra.freq_scale);
+    }
+    return make_float2(cosf(ang) * mag, sinf(ang) * mag);
+}
+
+__global__ void __launch_bounds__(KVT_THREADS)
 kvwrite_tail_kernel(float* __restrict__ kcur, const float* __restrict__ nw,
                     __half* __restrict__ kcache, int64_t row_stride, int64_t n_rows,
                     const int64_t* __restrict__ kidx, const int32_t* __restrict__ posv,
                     RopeArgs ra, int slab, int64_t slab_base) {
-    __shared__ float s_red[KVW_ROW / 32];
-    __shared__ float s_ss;
-    const int tid = threadIdx.x;
+    __shared__ float s_sumsq[KVT_LAT_PAIRS / 32];
+    const int t = threadIdx.x;
+    const int wp = t >> 5;
     pdl_wait();
-    const int64_t grow = kidx[0];
-    const int64_t row = slab ? grow - slab_base : grow;   // row of this GPU's cache
-    const int pos = posv[0];
-    float v = 0.0f, ss = 0.0f;
-    if (tid < KVW_LAT) {
-        v = kcur[tid];
-        ss = v * v;
+    const int64_t cache_row = kidx[0];
+    const int64_t local_row = slab ? cache_row - slab_base : cache_row;
+    float2* kc2 = reinterpret_cast<float2*>(kcur);
+    const float2 pr = kc2[t];                 // this thread's pair of pre-norm values
+    float sumsq = t < KVT_LAT_PAIRS ? pr.x * pr.x + pr.y * pr.y : 0.0f;
+    sumsq = warp_sum(sumsq);
+    if (wp < KVT_LAT_PAIRS / 32 && (t & 31) == 0) s_sumsq[wp] = sumsq;
+    float2 res;
+    if (t < KVT_LAT_PAIRS) {
+        const float2 g = reinterpret_cast<const float2*>(nw)[t];
+        __syncthreads();
+        float tot = 0.0f;
+#pragma unroll
+        for (int w = 0; w < KVT_LAT_PAIRS / 32; ++w) tot += s_sumsq[w];
+        const float inv_rms = rsqrtf(tot / static_cast<float>(KVW_LAT) + ra.eps);
+        res = make_float2(pr.x * inv_rms * g.x, pr.y * inv_rms * g.y);
+    } else {
+        const float2 cs = yarn_rotation(ra, posv[0], t - KVT_LAT_PAIRS);
+        __syncthreads();
+        res = make_float2(pr.x * cs.x - pr.y * cs.y, pr.x * cs.y + pr.y * cs.x);
     }
-    const float t = warp_sum(ss);
-    if ((tid & 31) == 0) s_red[tid >> 5] = t;
-    __syncthreads();
-    if (tid == 0) {
-        float s = 0.0f;
-        for (int i = 0; i < KVW_ROW / 32; ++i) s += s_red[i];
-        s_ss = s;
-    }
-    __syncthreads();
-    const float scale = rsqrtf(s_ss / static_cast<float>(KVW_LAT) + ra.eps);
-
-    float x0 = 0.0f, x1 = 0.0f, co = 0.0f, si = 0.0f;
-    const bool is_rope = tid >= KVW_LAT && tid < KVW_LAT + KVW_ROPE / 2;
-    if (is_rope) {
-        const int p = tid - KVW_LAT;
-        x0 = kcur[KVW_LAT + 2 * p];
-        x1 = kcur[KVW_LAT + 2 * p + 1];
-        const float theta_extrap = static_cast<float>(pos) * powf(ra.theta_scale, static_cast<float>(p));
-        float mscale = ra.attn_factor;
-        float theta = ra.freq_scale * theta_extrap;
-        if (ra.ext_factor != 0.0f) {
-            const float y = (static_cast<float>(p) - ra.corr0) / fmaxf(0.001f, ra.corr1 - ra.corr0);
-            const float mix = (1.0f - fminf(1.0f, fmaxf(0.0f, y))) * ra.ext_factor;
-            theta = theta * (1.0f - mix) + theta_extrap * mix;
-            mscale *= 1.0f + 0.1f * logf(1.0f / ra.freq_scale);
-        }
-        co = cosf(theta) * mscale;
-        si = sinf(theta) * mscale;
-    }
-    __syncthreads();   // every thread has read its inputs before Kcur is overwritten
-    if (tid < KVW_LAT) kcur[tid] = scale * v * nw[tid];
-    if (is_rope) {
-        const int p = tid - KVW_LAT;
-        kcur[KVW_LAT + 2 * p] = x0 * co - x1 * si;
-        kcur[KVW_LAT + 2 * p + 1] = x0 * si + x1 * co;
-    }
-    __syncthreads();
-    if (row < 0 || row >= n_rows) {
+    kc2[t] = res;                             // each thread rewrites only the pair it read
+    if (local_row >= 0 && local_row < n_rows) {
+        reinterpret_cast<__half2*>(kcache + local_row * row_stride)[t] = __float22half2_rn(res);
+    } else if (t == 0 && (!slab || cache_row < 0)) {
         // one cache: a row outside it is an error; a slab: only a negative row is, any other row
         // belongs to another GPU's slab
-        if (tid == 0 && (!slab || grow < 0)) atomicExch(&g_status, DEV_STATUS_BADSEQ);
-        return;
+        atomicExch(&g_status, DEV_STATUS_BADSEQ);
     }
-    kcache[row * row_stride + tid] = __float2half(kcur[tid]);
 }
 
 }  // namespace q8
@@ -292,7 +298,7 @@ cudaError_t launch_kvwrite(const KvWriteLaunch& a, cudaStream_t stream) {
                            a.cur, static_cast<const uint8_t*>(a.w), a.kcur);
     if (e != cudaSuccess) return e;
     RopeArgs ra = {a.eps, a.freq_scale, a.ext_factor, a.attn_factor, a.theta_scale, a.corr0, a.corr1};
-    return launch(kvwrite_tail_kernel, dim3(1), dim3(KVW_ROW), 0, stream, a.flags | M4B_FLAG_PDL,
+    return launch(kvwrite_tail_kernel, dim3(1), dim3(KVT_THREADS), 0, stream, a.flags | M4B_FLAG_PDL,
                   a.kcur, a.norm_w, static_cast<__half*>(a.kcache), a.kcache_row_stride,
                   a.kcache_rows, a.kidx, a.pos, ra, a.slab, a.slab_base);
 }

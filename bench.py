@@ -2,14 +2,16 @@
 """bench.py -- MLA decode-attention layer-steps/s on B200 for aubier's fused M4 path.
 
 Workload (the default): one decode token over a 262,144-key latent+rope f16 KV
-cache, 36 layers, each with its own seeded W_UK / W_UV / cache; 32 heads, q_nope 128, rope 64,
-latent 512, V head 128, kq_scale 1/sqrt(192).  One step = the 36 layer-steps WKB -> KQKV ->
-PHASE(combine + W_UV), captured in one CUDA graph.  With N GPUs the 262,144 keys of every layer
-are split into N contiguous slabs (strong scaling): each rank computes split-K partials over its
-slab, merges them into one record per head and stores it into every peer over NVLink (fused
-exchange; --exchange nccl uses an NCCL all-gather instead), then merges all ranks' records and
-applies W_UV.
+cache, 36 layers, each with its own seeded W_UK / W_UV / cache and its own f32 window mask (the
+engine's, resident on the device); 32 heads, q_nope 128, rope 64, latent 512, V head 128,
+kq_scale 1/sqrt(192).  One step = the 36 layer-steps WKB -> KQKV -> PHASE(combine + W_UV),
+captured in one CUDA graph.  With N GPUs the 262,144 keys of every layer are split into N
+contiguous slabs (strong scaling): each rank computes split-K partials over its slab, merges them
+into one record per head and stores it into every peer over NVLink (fused exchange; --exchange
+nccl uses an NCCL all-gather instead), then merges all ranks' records and applies W_UV.
 
+--config 2 / 3: the same step at 4,096 / 32,768 keys (at N=1 the default run also measures both
+and reports them under "other_configs").
 --config 5: ragged batched decode, 16 sequences with one new token each, lengths uniform on
 [512, 65536] by seed, one packed cache per layer with per-sequence base/length; whole sequences
 per rank (LPT on keys), no exchange.  A layer-step covers all 16 sequences.
@@ -18,9 +20,11 @@ Printed JSON line (rank 0): value = layer-steps/s of the whole job, timed on the
 ranks) around exactly --steps graph replays; e2e = the same metric with the step's queries copied
 host->device and its outputs device->host inside the timed region; roofline = the KQKV kernel's
 algorithmic bytes per launch over its CUDA-event-timed average launch, against the measured HBM
-copy peak; cpu_baseline = the reference's own unfused CPU ggml graph (oracle/_ref) on this host.
+copy peak; cpu_baseline = the reference's own unfused CPU ggml graph (oracle/_ref) on this host,
+median of >= 20 layer-steps; parity = the last layer of one more step against a float64
+evaluation of the same inputs (slabs gathered from every rank), outside the timed region.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 4|5]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5]
 """
 from __future__ import annotations
 
@@ -43,14 +47,17 @@ D, DQ = R + ROPE, NOPE + ROPE
 SCALE = 1.0 / math.sqrt(DQ)
 PART = R + 4
 METRIC = "MLA decode attn layer-steps/s (262144 keys, 36 layers)"
+METRIC_KEYS = "MLA decode attn layer-steps/s ({keys} keys, 36 layers)"
+CONFIG_KEYS = {2: 4096, 3: 32768, 4: 262144}
 METRIC5 = "MLA decode attn layer-steps/s (16 ragged sequences, 36 layers)"
 METRIC_M = "MLA decode attn layer-steps/s (262144 keys, 36 layers, Mistral-Small-4 geometry)"
 UNIT = "layer-steps/s"
 
 
-def layer_bytes(n_keys: int) -> int:
-    """Algorithmic bytes of one layer-step: KV once, weights once, q and the output (no mask)."""
-    return 1152 * n_keys + 2 * (H * R * NOPE * 2) + H * DQ * 4 + H * V * 4
+def layer_bytes(n_keys: int, mask: bool = True) -> int:
+    """Algorithmic bytes of one layer-step: KV once, the f32 mask when the op consumes it, weights
+    once, q and the output."""
+    return (1152 + (4 if mask else 0)) * n_keys + 2 * (H * R * NOPE * 2) + H * DQ * 4 + H * V * 4
 
 
 def measured_peak():
@@ -142,32 +149,35 @@ def _ref_graph(n_keys: int, threads: int, seed: int):
     return ref
 
 
-def cpu_reference(lengths, reps: int, warmup: int = 1, budget_s: float = 60.0):
+def cpu_reference(lengths, reps: int = 20, warmup: int = 1, budget_s: float = 30.0):
     """The reference's CPU graph for one layer-step of the workload: one single-token graph per
-    sequence (config 4: one sequence of 262,144 keys), all host threads."""
+    sequence (config 4: one sequence of 262,144 keys), all host threads.  At least ``reps``
+    layer-steps when they fit in about ``budget_s`` seconds (never fewer than 3); the value is
+    the median over the timed layer-steps."""
     from oracle import oracle as O
     threads = os.cpu_count() or 1
     refs = [_ref_graph(n, threads, 4 + i) for i, n in enumerate(lengths)]
     for _ in range(warmup):
         for r in refs:
             r.compute()
-    t0 = time.perf_counter()
-    done = 0
-    while done < reps:        # bounded: at most `reps` layer-steps or about budget_s seconds
+    times = []
+    t_all = time.perf_counter()
+    while len(times) < reps:
+        t0 = time.perf_counter()
         for r in refs:
             r.compute()
-        done += 1
-        if time.perf_counter() - t0 > budget_s:
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 3 and time.perf_counter() - t_all > budget_s:
             break
-    dt = time.perf_counter() - t0
     for r in refs:
         r.close()
+    med = statistics.median(times)
     what = (f"{lengths[0]} keys" if len(lengths) == 1 else
             f"{len(lengths)} sequences, {sum(lengths)} keys in all")
-    return {"value": done / dt, "unit": UNIT, "cores": threads, "kind": "reference",
-            "sample": f"{done} x 1 layer-step ({what}; unfused ggml-cpu graph of "
+    return {"value": 1.0 / med, "unit": UNIT, "cores": threads, "kind": "reference",
+            "sample": f"median of {len(times)} x 1 layer-step ({what}; unfused ggml-cpu graph of "
                       f"engine/m1_layer.cpp:437-502, {O.ref_library_path().rsplit('/', 1)[-1]})",
-            "s_per_layer_step": dt / done, "reps": done}
+            "s_per_layer_step": med, "reps": len(times)}
 
 
 def workload_lengths(args):
@@ -177,16 +187,22 @@ def workload_lengths(args):
     return [args.keys]
 
 
+def metric_of(args):
+    if args.config == 5:
+        return METRIC5
+    return METRIC if args.keys == 262144 else METRIC_KEYS.format(keys=args.keys)
+
+
 def run_reference(args, rank: int) -> None:
     if rank != 0:
         return
     try:
-        cb = cpu_reference(workload_lengths(args), reps=args.steps, warmup=args.warmup)
+        cb = cpu_reference(workload_lengths(args), reps=max(20, args.steps), warmup=args.warmup,
+                           budget_s=120.0)
     except Exception as e:   # the oracle library travels prebuilt; report if it does not load
         print(json.dumps({"impl": "reference", "unavailable": f"oracle/_ref not loadable: {e}"}))
         return
-    metric = METRIC if args.config == 4 else METRIC5
-    line = {"impl": "reference", "metric": metric, "value": cb["value"], "unit": UNIT,
+    line = {"impl": "reference", "metric": metric_of(args), "value": cb["value"], "unit": UNIT,
             "n_gpus": args.gpus, "steps": cb["reps"], "warmup": args.warmup,
             "ms_per_step": 1e3 / cb["value"], "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
@@ -223,8 +239,10 @@ def _layer_weights(L, dev):
 
 
 def slab_workload(args, rank, world, dev):
-    """Config 4: one token, 262,144 keys per layer, cut into one contiguous slab per rank; the
-    per-head records cross GPUs once per layer (fused NVLink exchange, or NCCL)."""
+    """Configs 2-4: one token, N keys per layer (4,096 / 32,768 / 262,144), cut into one
+    contiguous slab per rank; the per-head records cross GPUs once per layer (fused NVLink
+    exchange, or NCCL).  Every layer's KQKV consumes its own f32 mask -- the engine's mask for the
+    window [0, N) (m1_layer.cpp:756-773), resident on the device -- as the engine's graph does."""
     import torch
     import torch.distributed as dist
     from aubier_b200 import m4
@@ -233,7 +251,7 @@ def slab_workload(args, rank, world, dev):
     n_loc = N // world
     S = m4.default_splits(n_loc)
     wuk, wuv, g = _layer_weights(L, dev)
-    kc, qcur = [], []
+    kc, qcur, mask = [], [], []
     q = torch.empty(L, H, DQ, device=dev)
     for layer in range(L):
         g.manual_seed(1000 * layer + 11 + 100003 * rank)   # weights replicated, slabs differ
@@ -243,6 +261,7 @@ def slab_workload(args, rank, world, dev):
         qc = torch.empty(H, D, device=dev)
         qc[:, R:] = q[layer][:, NOPE:]
         qcur.append(qc)
+        mask.append(torch.zeros(n_loc, device=dev))
     w = Workload()
     part = torch.empty(S, H, PART, device=dev)
     merged = torch.empty(1, H, PART, device=dev)
@@ -261,7 +280,7 @@ def slab_workload(args, rank, world, dev):
         for layer in range(L):
             # WKB writes q_abs and (QCAT) the query's rope half: Qcur = concat(q_abs, q_pe)
             m4.wkb(wuk[layer], q[layer][:, :NOPE], out=qcur[layer][:, :R], flags=flags | m4.FLAG_QCAT)
-            m4.kqkv_partials(kc[layer], qcur[layer], None, SCALE, out=part,
+            m4.kqkv_partials(kc[layer], qcur[layer], mask[layer], SCALE, out=part,
                              flags=flags | m4.FLAG_KV_STATIC)
             if xchg is not None:   # one launch: merge, NVLink stores into every peer, wait, merge, W_UV
                 xchg.merge_wvb(part, wuv[layer], out=w.out[layer], attn_out=attn, flags=flags)
@@ -273,33 +292,80 @@ def slab_workload(args, rank, world, dev):
 
     def kq():
         for layer in range(L):
-            m4.kqkv_partials(kc[layer], qcur[layer], None, SCALE, out=part,
+            m4.kqkv_partials(kc[layer], qcur[layer], mask[layer], SCALE, out=part,
                              flags=m4.FLAG_PDL | m4.FLAG_KV_STATIC)
 
-    w.step, w.kq = step, kq
+    def parity():
+        """The last layer of the step just run (its attention is still in ``attn``) against a
+        float64 evaluation of the same inputs on rank 0, the slabs gathered from every rank."""
+        layer = L - 1
+        if world > 1:
+            full = torch.empty(world * n_loc, D, dtype=kc[layer].dtype, device=dev)
+            dist.all_gather_into_tensor(full, kc[layer])
+        else:
+            full = kc[layer]
+        if rank != 0:
+            return None
+        xa, xo = fp64_layer_torch(q[layer], wuk[layer], full, wuv[layer])
+        return {"layer": layer, "keys": N,
+                "rel_err_out": _rel_to_max(w.out[layer], xo),
+                "rel_err_attn": _rel_to_max(attn, xa), "tol": 2e-3,
+                "ref": "float64 torch evaluation of the same inputs (q and Qcur rounded to f16 "
+                       "as the tensor cores and the CPU graph's mul_mat round them; attention "
+                       "rounded to f16 before W_UV)"}
+
+    w.step, w.kq, w.parity = step, kq, parity
     w.kq_kernel = "kqkv_partial_kernel"
-    w.kq_bytes = 1152 * n_loc + H * D * 4
+    w.kq_bytes = (1152 + 4) * n_loc + H * D * 4
     w.job_layer_bytes = layer_bytes(N)
     # WKB, partials, merge + W_UV (one launch; with the fused exchange, the exchange too); the
     # NCCL variant adds the local record merge (NCCL's own kernel is not counted)
     w.launches_per_step = (3 if (world == 1 or xchg is not None) else 4) * L
-    w.traffic = profiled_traffic("kqkv_partial_n262144.md")
+    w.traffic = profiled_traffic("kqkv_partial_n262144.md") if N == 262144 else None
     if w.traffic is not None and world > 1:
         w.traffic = w.traffic / world        # the committed capture is of the 1-GPU slab
-    w.metric = METRIC
-    w.config = {"workload": "BASELINE config 4: 1 decode token, 262144-key f16 latent+rope KV "
-                            "cache, 36 layers, 32 heads, nope 128 / rope 64 / latent 512 / V 128",
+    cfg = {4096: 2, 32768: 3, 262144: 4}.get(N)
+    w.metric = METRIC if N == 262144 else METRIC_KEYS.format(keys=N)
+    w.config = {"workload": (f"BASELINE config {cfg}: " if cfg else "") +
+                            f"1 decode token, {N}-key f16 latent+rope KV cache, {L} layers, 32 "
+                            "heads, nope 128 / rope 64 / latent 512 / V 128",
                 "keys": N, "layers": L, "keys_per_gpu": n_loc, "splits_per_gpu": S,
+                "mask": "f32 [N] per layer, the engine's window mask, resident on the device "
+                        "and read by every KQKV launch",
                 "parallelism": f"kv-slab x{world}" + (
                     "" if world == 1 else
                     " + fused NVLink record exchange" if xchg is not None else
                     " + nccl all-gather of merged records"),
-                "l2": "inputs larger than L2 (36 layers x 302 MB KV per step)",
+                "l2": f"inputs larger than L2 ({L} layers x {1156 * N / 1e6:.1f} MB KV + mask "
+                      "per step)",
                 "step": "WKB -> KQKV split-K partials -> PHASE combine+W_UV per layer, "
                         "one CUDA graph per step"}
     w.close = (lambda: xchg.close()) if xchg is not None else (lambda: None)
     w.lengths = [N]
     return w
+
+
+def fp64_layer_torch(q, w_uk, kc, w_uv):
+    """One layer step in float64 on the device, the arbiter of the bench's parity line: q_nope
+    and Qcur rounded to f16 (the tensor-core operands; the reference CPU graph's mul_mat rounds
+    its f32 src1 to f16 the same way), the attention rounded to f16 before W_UV, all sums in
+    float64.  q (H, 192) f32, w_uk (H, 512, 128) f16, kc (N, 576) f16, w_uv (H, 128, 512) f16."""
+    import torch
+    f64 = torch.float64
+    qn = q[:, :NOPE].half().to(f64)
+    qabs = torch.einsum("hrk,hk->hr", w_uk.to(f64), qn)
+    qc = torch.cat([qabs, q[:, NOPE:].to(f64)], 1).half().to(f64)
+    K = kc.to(f64)
+    p = torch.softmax((K @ qc.T) * SCALE, dim=0)       # (N, H)
+    attn = p.T @ K[:, :R]
+    out = torch.einsum("hvr,hr->hv", w_uv.to(f64), attn.half().to(f64))
+    return attn, out
+
+
+def _rel_to_max(x, ref) -> float:
+    import torch
+    d = (x.to(torch.float64) - ref).abs().max()
+    return float(d / ref.abs().max().clamp_min(1e-300))
 
 
 def _q8_bytes(rows: int, K: int, g, dev):
@@ -364,7 +430,22 @@ def mistral_workload(args, rank, world, dev):
             m4.kqkv_partials(kc[layer], qcur[layer], None, scale, out=part,
                              flags=m4.FLAG_PDL | m4.FLAG_KV_STATIC)
 
-    w.step, w.kq = step, kq
+    def parity():
+        """The last layer's attention (after its KV-write) against a float64 evaluation from the
+        same Qcur; the Q8_0 gemvs around it follow the fused reference's Q8_1 numerics and are
+        checked against their restatement by the test suite, not here."""
+        import torch
+        layer = L - 1
+        f64 = torch.float64
+        qc = qcur[layer].half().to(f64)
+        K = kc[layer].to(f64)
+        p = torch.softmax((K @ qc.T) * scale, dim=0)
+        xa = p.T @ K[:, :RM]
+        return {"layer": layer, "keys": N, "rel_err_attn": _rel_to_max(attn, xa), "tol": 2e-3,
+                "ref": "float64 torch evaluation of the attention from the same Qcur (rounded to "
+                       "f16) and the cache after the KV-write"}
+
+    w.step, w.kq, w.parity = step, kq, parity
     w.kq_kernel = "kqkv_partial_kernel<Geo<256>>"
     w.kq_bytes = 640 * N + H * DM * 4
     w.job_layer_bytes = (640 * N + H * RM * 68 + H * V * 272 + DM * 4352 + 4096 * 4 + H * DQM * 4
@@ -390,6 +471,7 @@ def ragged_workload(args, rank, world, dev):
     layer's cache packed with per-sequence base/length; whole sequences per rank (LPT on keys),
     no exchange."""
     import torch
+    import torch.distributed as dist
     from aubier_b200 import m4
     from aubier_b200.shard import lpt_assign, packed_bases, ragged_lengths
     L = args.layers
@@ -433,7 +515,31 @@ def ragged_workload(args, rank, world, dev):
             m4.kqkv_ragged(kc[layer], qcur[layer], base, length, SCALE, out=attn, scratch=scratch,
                            flags=m4.FLAG_PDL | m4.FLAG_KV_STATIC)
 
-    w.step, w.kq = step, kq
+    def parity():
+        """Every token of this rank in the last layer of the step just run against a float64
+        evaluation of its window; the worst gap over all ranks is reported by rank 0."""
+        layer = L - 1
+        worst = torch.zeros(4, dtype=torch.float64, device=dev)   # max|d attn|, max|attn|, out ...
+        bases = packed_bases(my_len)
+        for t in range(T):
+            kt = kc[layer][bases[t]:bases[t] + my_len[t]]
+            xa, xo = fp64_layer_torch(q[layer][t], wuk[layer], kt, wuv[layer])
+            v = torch.stack([(attn[t].double() - xa).abs().max(), xa.abs().max(),
+                             (w.out[layer][t].double() - xo).abs().max(), xo.abs().max()])
+            worst = torch.maximum(worst, v)
+        if world > 1:
+            dist.all_reduce(worst, op=dist.ReduceOp.MAX)
+        if rank != 0:
+            return None
+        wv = worst.tolist()
+        return {"layer": layer, "tokens": len(lengths), "keys": sum(lengths),
+                "rel_err_out": wv[2] / wv[3], "rel_err_attn": wv[0] / wv[1], "tol": 2e-3,
+                "ref": "float64 torch evaluation of every token's window (q and Qcur rounded to "
+                       "f16 as the tensor cores and the CPU graph's mul_mat round them; attention "
+                       "rounded to f16 before W_UV); max gap over all tokens and ranks over the "
+                       "max reference value"}
+
+    w.step, w.kq, w.parity = step, kq, parity
     w.kq_kernel = "kqkv_partial_kernel (ragged) + kqkv_ragged_combine_kernel"
     w.kq_bytes = 1152 * rows + T * H * D * 4
     w.job_layer_bytes = 1152 * sum(lengths) + 2 * (H * R * NOPE * 2) + len(lengths) * (
@@ -455,21 +561,25 @@ def ragged_workload(args, rank, world, dev):
     return w
 
 
-def run_ours(args, rank: int, world: int) -> None:
+def measure(w, args, rank: int, world: int, dev, sample_clocks: bool = True) -> dict:
+    """Warm up, capture one CUDA graph per step, time exactly --steps replays (barrier and
+    synchronize on both sides, max over ranks), then the e2e variant, the dominant kernel alone
+    and the parity check of one freshly computed step.  Every rank takes the same collective
+    steps in the same order."""
     import torch
     import torch.distributed as dist
     from aubier_b200 import m4
-
-    dev = torch.device("cuda", torch.cuda.current_device())
     L = args.layers
-    if args.geometry == "mistral":
-        w = mistral_workload(args, rank, world, dev)
-    else:
-        w = (ragged_workload if args.config == 5 else slab_workload)(args, rank, world, dev)
 
     def barrier():
         if world > 1:
             dist.barrier()
+
+    def max_over_ranks(ms):
+        t = torch.tensor([ms], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
     # ---- eager warm-up, then one CUDA graph per step
     stream = torch.cuda.Stream()
@@ -489,7 +599,7 @@ def run_ours(args, rank: int, world: int) -> None:
     assert status == m4.OK, f"device status {status}"
 
     # ---- timed region: exactly --steps replays, barrier + synchronize on both sides
-    sampler = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    sampler = ClockSampler(torch.cuda.current_device()) if (rank == 0 and sample_clocks) else None
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     if sampler:
@@ -504,12 +614,9 @@ def run_ours(args, rank: int, world: int) -> None:
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop() if sampler else None
-    t = torch.tensor([e0.elapsed_time(e1)], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    ms_per_step = ms_max / args.steps
-    value = L * args.steps / (ms_max * 1e-3)
+    ms_max = max_over_ranks(e0.elapsed_time(e1))
+    r = {"ms_per_step": ms_max / args.steps, "value": L * args.steps / (ms_max * 1e-3),
+         "clocks": clocks}
 
     # ---- end to end: host queries in, host outputs back, every step
     q_host = torch.randn((args.steps,) + tuple(w.q.shape), pin_memory=True)
@@ -529,12 +636,10 @@ def run_ours(args, rank: int, world: int) -> None:
     e1.record()
     torch.cuda.synchronize()
     barrier()
-    te = torch.tensor([e0.elapsed_time(e1)], device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = L * args.steps / (float(te.item()) * 1e-3)
-    h2d = w.q.numel() * 4 * world      # whole job: every rank copies its own queries
-    d2h = w.out.numel() * 4 * world
+    r["e2e"] = {"value": L * args.steps / (max_over_ranks(e0.elapsed_time(e1)) * 1e-3),
+                "unit": UNIT,
+                "h2d_bytes_per_step": w.q.numel() * 4 * world,   # every rank copies its queries
+                "d2h_bytes_per_step": w.out.numel() * 4 * world}
 
     # ---- the dominant kernel alone: one graph of its L launches, CUDA events around it
     graph_kq = torch.cuda.CUDAGraph()
@@ -551,39 +656,87 @@ def run_ours(args, rank: int, world: int) -> None:
     kq_us = e0.elapsed_time(e1) * 1e3 / (kreps * L)
     peak, peak_kind = measured_peak()
     achieved = w.kq_bytes / (kq_us * 1e-6) / 1e9
-
+    r["roofline"] = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": w.traffic, "peak_kind": peak_kind,
+                     "kernel": w.kq_kernel, "kernel_us": kq_us,
+                     "bytes_per_launch": w.kq_bytes,
+                     "frac_of_nominal_8000": achieved / 8000.0}
+    r["hbm_gbs_step"] = L * w.job_layer_bytes / (r["ms_per_step"] * 1e-3) / 1e9
     assert m4.device_status() == m4.OK
     del graph, graph_e2e, graph_kq           # release graphs before the process group
+
+    # ---- parity: one eager step, its last layer against a float64 evaluation (outside timing)
+    w.step()
+    torch.cuda.synchronize()
+    assert m4.device_status() == m4.OK
+    r["parity"] = w.parity()
+    return r
+
+
+def cpu_baseline_of(lengths, reps):
+    try:
+        cb = cpu_reference(lengths, reps=reps)
+        return {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    except Exception as e:
+        return {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
+                "sample": f"unavailable: {e}"}
+
+
+def run_ours(args, rank: int, world: int) -> None:
+    import copy
+
+    import torch
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if args.geometry == "mistral":
+        w = mistral_workload(args, rank, world, dev)
+    else:
+        w = (ragged_workload if args.config == 5 else slab_workload)(args, rank, world, dev)
+    r = measure(w, args, rank, world, dev)
     w.close()                                # collective where the workload exchanges
+    lengths, metric, config = w.lengths, w.metric, w.config
+    launches = w.launches_per_step * args.steps
+    del w
+    torch.cuda.empty_cache()
+
+    # configs 2 and 3 (4,096 and 32,768 keys, 36 layers) beside the headline, on one GPU
+    others = []
+    if (world == 1 and args.config == 4 and args.geometry == "baseline" and args.keys == 262144
+            and not args.no_other_configs):
+        for cfg in (2, 3):
+            a2 = copy.copy(args)
+            a2.keys = CONFIG_KEYS[cfg]
+            w2 = slab_workload(a2, rank, world, dev)
+            r2 = measure(w2, a2, rank, world, dev, sample_clocks=False)
+            r2 = {"config": cfg, "metric": w2.metric, "value": r2["value"], "unit": UNIT,
+                  "ms_per_step": r2["ms_per_step"], "e2e": r2["e2e"], "roofline": r2["roofline"],
+                  "hbm_gbs_step": r2["hbm_gbs_step"], "parity": r2["parity"],
+                  "workload": w2.config["workload"]}
+            if not args.no_cpu_baseline:
+                r2["cpu_baseline"] = cpu_baseline_of(w2.lengths, 20)
+            others.append(r2)
+            del w2
+            torch.cuda.empty_cache()
 
     if rank != 0:
         return
-    cpu_baseline = None
     _restore_stdout()
-    if world == 1 and not args.no_cpu_baseline and w.lengths is not None:
-        try:
-            cb = cpu_reference(w.lengths, reps=args.cpu_reps)
-            cpu_baseline = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
-        except Exception as e:
-            cpu_baseline = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
-                            "sample": f"unavailable: {e}"}
-    step_gbs = L * w.job_layer_bytes / (ms_per_step * 1e-3) / 1e9
+    cpu_baseline = None
+    if world == 1 and not args.no_cpu_baseline and lengths is not None:
+        cpu_baseline = cpu_baseline_of(lengths, args.cpu_reps)
+        if args.config == 4 and args.geometry == "baseline":
+            # config 1: the reference's own CPU-runnable case, 256 keys, 1 layer-step
+            cpu_baseline["config1"] = cpu_baseline_of([256], 200)
     line = {
-        "metric": w.metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": w.config,
-        "hbm_gbs_step": step_gbs,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": w.traffic, "peak_kind": peak_kind,
-                     "kernel": w.kq_kernel, "kernel_us": kq_us,
-                     "frac_of_nominal_8000": achieved / 8000.0},
-        "cpu_baseline": cpu_baseline,
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
-        "gpu_launches": w.launches_per_step * args.steps,
-        "clocks": clocks,
+        "metric": metric, "value": r["value"], "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic", "config": config, "hbm_gbs_step": r["hbm_gbs_step"],
+        "roofline": r["roofline"], "cpu_baseline": cpu_baseline, "e2e": r["e2e"],
+        "gpu_launches": launches, "clocks": r["clocks"], "parity": r["parity"],
     }
+    if others:
+        line["other_configs"] = others
     print(json.dumps(line), flush=True)
 
 
@@ -614,17 +767,23 @@ def main():
     ap.add_argument("--steps", type=int, default=150)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--keys", type=int, default=262144)
+    ap.add_argument("--keys", type=int, default=None,
+                    help="keys per layer (default: the config's, 262,144 for config 4)")
     ap.add_argument("--layers", type=int, default=36)
-    ap.add_argument("--cpu-reps", type=int, default=3)
+    ap.add_argument("--cpu-reps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-other-configs", action="store_true",
+                    help="config 4 at N=1: skip the configs 2 and 3 lines beside the headline")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="config 4, N>1: fused NVLink exchange in the merge kernels, or NCCL")
-    ap.add_argument("--config", type=int, choices=[4, 5], default=4,
-                    help="4: 262,144-key slabs (the headline); 5: 16 ragged sequences")
+    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=4,
+                    help="2/3/4: 4,096 / 32,768 / 262,144-key slabs (4 is the headline); "
+                         "5: 16 ragged sequences")
     ap.add_argument("--geometry", choices=["baseline", "mistral"], default="baseline",
                     help="mistral: config 4 at the reference's own model geometry (1 GPU)")
     args = ap.parse_args()
+    if args.keys is None:
+        args.keys = CONFIG_KEYS.get(args.config, 262144)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
