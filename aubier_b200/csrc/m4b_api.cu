@@ -608,6 +608,18 @@ int m4b_supports_op(int op, const m4b_tensor* srcs, int n_srcs, const m4b_tensor
         }
         case 1: {
             if (n_srcs < 2) return 0;
+            if (n_srcs >= 5 && srcs[3].data != nullptr) {   // the ragged batch form
+                if (n_srcs > 2 && srcs[2].data != nullptr) return 0;   // windows, not a mask
+                m4b_kqkv_ragged_args r;
+                std::memset(&r, 0, sizeof(r));
+                r.kcache = srcs[0];
+                r.q = srcs[1];
+                r.seq_base = srcs[3];
+                r.seq_len = srcs[4];
+                r.dst = *dst;
+                r.kq_scale = op_params ? *reinterpret_cast<const float*>(op_params) : 1.0f;
+                return check_kqkv_ragged(r, &geom) == M4B_OK;
+            }
             m4b_kqkv_args a;
             std::memset(&a, 0, sizeof(a));
             a.src0 = srcs[0];

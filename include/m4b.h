@@ -282,8 +282,12 @@ M4B_API int      m4b_kqkv_max_splits(void);
 
 /*
  * The reference's supports_op (ggml-cuda.cu:5848-5885) for the three ops: 1 when the shapes and
- * types match a supported geometry (no launch, no CUDA call), 0 otherwise.  op: 0 = WKB,
- * 1 = KQKV, 2 = PHASE (phase from op_params[0]).  srcs: up to 6 operands, dst: the output.
+ * types match a supported geometry (no launch, no CUDA call, no memory read), 0 otherwise.
+ * op: 0 = WKB, 1 = KQKV, 2 = PHASE (phase from op_params[0]).  srcs: up to 6 operands, dst: the
+ * output.  A NULL data marks an absent optional operand; a present operand that has no memory yet
+ * (ggml asks while scheduling, before allocation) may carry any non-NULL, 256-byte-aligned
+ * placeholder.  KQKV with srcs[3] / srcs[4] present (and no mask) is the ragged batch form of
+ * m4b_kqkv_ragged: srcs[3] = seq_base, srcs[4] = seq_len, dst F32 [latent, T, 32].
  */
 M4B_API int m4b_supports_op(int op, const m4b_tensor * srcs, int n_srcs, const m4b_tensor * dst,
                     const int32_t * op_params);
