@@ -16,9 +16,9 @@
 // read twice: the K pass (all 576 columns, for MMA1) is released as soon as MMA1 consumed it,
 // and the V pass (the first 512 columns again, for MMA2) is re-read after the softmax -- from L2,
 // where the K pass left it (cache hint evict_last, re-read with evict_first).  HBM still sees
-// every KV byte once.  One FIFO ring of ten 16 KB chunks carries, in consumption order, the
-// chunks of K(i+1) and V(i) (interleaved), so MMA1 of tile i+1 runs while the softmax of tile i
-// works (S and P are double-buffered).
+// every KV byte once.  One FIFO ring of
+// five 32 KB slots carries, in consumption order, K(i+1) and V(i), so MMA1 of tile i+1 runs
+// while the softmax of tile i works (S and P are double-buffered).
 //
 // CTA = one split (a contiguous run of tiles, balanced as in m4-kqkv.cu:204-218), persistent,
 // one per SM.  Ragged batches (several tokens, each attending to its own window [base, base+len)
@@ -52,28 +52,13 @@ namespace kq {
 constexpr int H = kHeads;
 constexpr int TK = kTileKeys;           // 128 keys per tile
 constexpr int CHUNK_BYTES = TK * 128;   // 128 keys x 64 f16 columns = 16 KB, one SW128 TMA box
-// The ring: a FIFO of RING_CHUNKS 16 KB chunks holding variable-size entries, each a run of whole
-// chunks that one mbarrier pair tracks.  The K pass of a tile is cut into entries of up to
-// K_GROUP chunks, the V pass into entries of up to V_GROUP chunk pairs (one O^T block per pair).
-// Every entry costs the MMA issuer one barrier test, one fence and one commit (~400 cycles), so
-// fewer, larger entries cost less issue time; smaller ones let the ring refill sooner.  Measured
-// at 262,144 keys (same box, us per launch): 2-chunk K and V entries 71.7; 3-chunk K entries
-// 77.8; 3-chunk K + 4-chunk V 74.9; 5-chunk K + 4-chunk V 87.1; 1-chunk K 87-89; a 9-chunk ring
-// 1.7 % slower than 10.
-#ifndef M4B_KQ_RING_CHUNKS
-#define M4B_KQ_RING_CHUNKS 10
+constexpr int SLOT_BYTES = 2 * CHUNK_BYTES;
+constexpr int NSLOT = 5;                // FIFO ring: 5 x 32 KB
+// 1: each period's ring order puts half of tile i's V pass between tile i + 1's latent pairs and
+// its rope chunk, so the HBM reads of the K pass are spread over the period (Geo::K_SPLIT).
+#ifndef M4B_KQ_INTERLEAVE
+#define M4B_KQ_INTERLEAVE 0
 #endif
-#ifndef M4B_KQ_K_GROUP
-#define M4B_KQ_K_GROUP 2
-#endif
-#ifndef M4B_KQ_V_GROUP
-#define M4B_KQ_V_GROUP 1
-#endif
-constexpr int RING_CHUNKS = M4B_KQ_RING_CHUNKS;
-constexpr int K_GROUP = M4B_KQ_K_GROUP;
-constexpr int V_GROUP = M4B_KQ_V_GROUP;
-constexpr int NBAR = 16;                // entry barrier pairs: more than the ring holds entries
-static_assert(RING_CHUNKS <= NBAR, "an entry's barriers are reused only after it was released");
 constexpr int QCH_BYTES = H * 128;      // 32 heads x 64 columns f16 = 4 KB
 constexpr int P_BYTES = 2 * QCH_BYTES;  // 32 heads x 128 keys f16 = 8 KB (double-buffered)
 constexpr int CTRL_BYTES = 2048;
@@ -88,14 +73,17 @@ struct Geo {
     static constexpr int D = R + kRope;                 // 576 or 320: the KV row
     static constexpr int NCOL = D / 64;                 // 9 or 5 column chunks per key row
     static constexpr int LAT_PAIRS = R / 128;           // 4 or 2
-    static constexpr int K_ENTRIES = (NCOL + K_GROUP - 1) / K_GROUP;      // latent + rope chunks
-    static constexpr int V_ENTRIES = (LAT_PAIRS + V_GROUP - 1) / V_GROUP;  // latent chunk pairs
-    static_assert(K_GROUP <= RING_CHUNKS && 2 * V_GROUP <= RING_CHUNKS, "entries fit the ring");
+    static constexpr int K_ENTRIES = LAT_PAIRS + 1;     // chunk pairs, then the rope chunk
+    static constexpr int V_ENTRIES = LAT_PAIRS;
+    // Ring order of one period (tile i's V pass, tile i + 1's K pass): K entries [0, K_SPLIT),
+    // V entries [0, V_SPLIT), K entries [K_SPLIT, K_ENTRIES), V entries [V_SPLIT, V_ENTRIES).
+    static constexpr int K_SPLIT = M4B_KQ_INTERLEAVE ? LAT_PAIRS : K_ENTRIES;
+    static constexpr int V_SPLIT = M4B_KQ_INTERLEAVE ? V_ENTRIES / 2 : 0;
     static constexpr int PART = R + 4;                  // record: o[R], m, l, 2 pad
     static constexpr int PM = R;
     static constexpr int PL = R + 1;
     static constexpr int OFF_RING = 0;
-    static constexpr int OFF_Q = OFF_RING + RING_CHUNKS * CHUNK_BYTES;
+    static constexpr int OFF_Q = OFF_RING + NSLOT * SLOT_BYTES;
     static constexpr int OFF_P = OFF_Q + NCOL * QCH_BYTES;
     static constexpr int OFF_CTRL = OFF_P + 2 * P_BYTES;
     static constexpr int OFF_SEG = OFF_CTRL + CTRL_BYTES;
@@ -114,30 +102,6 @@ struct Geo {
 };
 using GeoBase = Geo<kLatent>;   // 512
 using GeoMistral = Geo<256>;
-
-// Consumption order of one period of the ring (tile i's V pass and tile i + 1's K pass): codes
-// k >= 0 are K entries of tile i + 1, codes -1 - v are V entries of tile i.  The first V entry
-// waits for P(i).  Interleaving spreads each period's HBM reads (K) between its L2 reads (V), so
-// the ring never holds only V chunks while the next tile's HBM stream waits for space.  Measured
-// at 262,144 keys (36 launches, same box): K(i+1) then V(i) 77.4-78.3 us; the order below
-// 75.2-75.5 us; other interleavings within 0.3 us of it.
-#ifndef M4B_KQ_SCHED
-#define M4B_KQ_SCHED 0, 1, 2, 3, -1, -2, 4, -3, -4
-#endif
-template <class G>
-struct Sched {
-    static constexpr int N = G::K_ENTRIES + G::V_ENTRIES;
-    __device__ static constexpr int at(int j) { return j < G::K_ENTRIES ? j : -1 - (j - G::K_ENTRIES); }
-};
-template <>
-struct Sched<GeoBase> {
-    static constexpr int N = GeoBase::K_ENTRIES + GeoBase::V_ENTRIES;
-    __device__ static constexpr int at(int j) {
-        constexpr int code[] = {M4B_KQ_SCHED};
-        static_assert(sizeof(code) / sizeof(code[0]) == N, "schedule covers every entry once");
-        return code[j];
-    }
-};
 
 constexpr int NTHREADS = 320;
 constexpr int TM_S = 0;
@@ -160,8 +124,8 @@ struct Seg {
 static_assert(sizeof(Seg) == 32, "segment table entry");
 
 struct Ctrl {
-    uint64_t full[NBAR];    // entry n: full[n % NBAR], phase n / NBAR (TMA bytes landed)
-    uint64_t empty[NBAR];   // entry n: empty[n % NBAR] (its MMAs completed: chunks reusable)
+    uint64_t full[NSLOT];
+    uint64_t empty[NSLOT];
     uint64_t s_full[2], p_full[2];
     uint64_t q_full, o_done, o_full;
     uint64_t red_full[2];   // per head group, once per tile: the 4 warps' flags / maxima are in
@@ -283,21 +247,6 @@ __device__ __forceinline__ int cut_owner(int T, int G, int t) {   // the CTA own
     return t < big ? t / (b + 1) : r + (t - big) / b;
 }
 
-// Placement of ring entries: both the producer and the MMA issuer walk the same entry sequence
-// through their own copy, so they agree on every entry's chunks without sharing state.  head counts
-// chunks allocated so far (monotonic), including the chunks skipped at the end of the ring when an
-// entry would not fit there: an entry never wraps, so its chunks are contiguous in shared memory.
-struct RingPlace {
-    uint32_t head = 0;
-    __device__ __forceinline__ uint32_t place(int nch) {   // monotonic start of the entry
-        const uint32_t off = head % RING_CHUNKS;
-        if (off + nch > RING_CHUNKS) head += RING_CHUNKS - off;
-        const uint32_t start = head;
-        head += nch;
-        return start;
-    }
-};
-
 struct KqParams {
     const float* q;
     int64_t q_hs;             // head stride, floats
@@ -326,7 +275,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
     const int ncta = gridDim.x;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < NBAR; ++i) {
+        for (int i = 0; i < NSLOT; ++i) {
             mbar_init(&C.full[i], 1);
             mbar_init(&C.empty[i], 1);
         }
@@ -416,32 +365,24 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
             if (!(p.flags & M4B_FLAG_KV_STATIC)) pdl_wait();
             const uint64_t pol_keep = l2_policy_evict_last();    // K pass: V is re-read soon
             const uint64_t pol_done = l2_policy_evict_first();   // V pass: last use
-            RingPlace ring;
-            uint32_t tail = 0;        // monotonic end of the entries released so far
-            uint32_t ends[NBAR];      // monotonic end of every entry in flight
-            int n = 0, oldest = 0;    // entries issued; the oldest one not yet released
+            int slot = 0, phase = 0, issued = 0;
             bool ok = true;
-            // one ring entry: chunks c0 .. c0 + nch - 1 of the tile at cache row key0
-            auto entry = [&](int key0, int c0, int nch, uint64_t pol) {
+            // one ring entry: chunks c0 (and c0 + 1 when two) of the tile at cache row key0
+            auto entry = [&](int key0, int c0, int two, uint64_t pol) {
+                ok = ok && mbar_wait(&C.empty[slot], phase ^ 1, abort_flag);
                 if (!ok) return;
-                const uint32_t start = ring.place(nch);
-                while (oldest < n && start + nch - tail > static_cast<uint32_t>(RING_CHUNKS)) {
-                    ok = mbar_wait(&C.empty[oldest % NBAR], (oldest / NBAR) & 1, abort_flag);
-                    if (!ok) return;
-                    tail = ends[oldest % NBAR];
-                    ++oldest;
+                mbar_arrive_expect_tx(&C.full[slot], two ? SLOT_BYTES : CHUNK_BYTES);
+                uint8_t* dst = smem + G::OFF_RING + slot * SLOT_BYTES;
+                tma_load_2d(dst, &tmap, 64 * c0, key0, &C.full[slot], pol);
+                if (two) tma_load_2d(dst + CHUNK_BYTES, &tmap, 64 * (c0 + 1), key0, &C.full[slot], pol);
+                ++issued;
+                if (++slot == NSLOT) {
+                    slot = 0;
+                    phase ^= 1;
                 }
-                ends[n % NBAR] = start + nch;
-                uint64_t* bar = &C.full[n % NBAR];
-                mbar_arrive_expect_tx(bar, nch * CHUNK_BYTES);
-                uint8_t* dst = smem + G::OFF_RING + (start % RING_CHUNKS) * CHUNK_BYTES;
-                for (int c = 0; c < nch; ++c)
-                    tma_load_2d(dst + c * CHUNK_BYTES, &tmap, 64 * (c0 + c), key0, bar, pol);
-                ++n;
             };
             int gk = 0, gv = 0;
-            // ring order = consumption order: K(0), then per period i the schedule's mix of
-            // K(i+1) and V(i) entries
+            // ring order = consumption order: K(0), then per tile i: K(i+1), V(i)
             for (int t = -1; t < NT && ok; ++t) {
                 int kkey = -1, vkey = -1;
                 if (t + 1 < NT) {
@@ -452,22 +393,25 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
                     const Seg& sg = seg_of(t, gv);
                     vkey = sg.row0 + (t - sg.first) * TK;
                 }
-#pragma unroll
-                for (int j = 0; j < Sched<G>::N; ++j) {
-                    const int c = Sched<G>::at(j);
-                    if (c >= 0 && kkey >= 0) {
-                        entry(kkey, K_GROUP * c, min(K_GROUP, G::NCOL - K_GROUP * c), pol_keep);
-                    } else if (c < 0 && vkey >= 0) {
-                        const int v = -1 - c;
-                        entry(vkey, 2 * V_GROUP * v, 2 * min(V_GROUP, G::LAT_PAIRS - V_GROUP * v),
-                              pol_done);
-                    }
-                }
+                auto kpart = [&](int e0, int e1) {
+                    if (kkey >= 0)
+                        for (int e = e0; e < e1; ++e) entry(kkey, 2 * e, e < G::LAT_PAIRS, pol_keep);
+                };
+                auto vpart = [&](int e0, int e1) {
+                    if (vkey >= 0)
+                        for (int e = e0; e < e1; ++e) entry(vkey, 2 * e, 1, pol_done);
+                };
+                kpart(0, G::K_SPLIT);
+                vpart(0, G::V_SPLIT);
+                kpart(G::K_SPLIT, G::K_ENTRIES);
+                vpart(G::V_SPLIT, G::V_ENTRIES);
             }
             if (*abort_flag) {
                 // let this CTA's own copies land before its shared memory is released
-                for (int m = n > NBAR ? n - NBAR : 0; m < n; ++m)
-                    mbar_drain(&C.full[m % NBAR], (m / NBAR) & 1);
+                for (int sl = 0; sl < NSLOT; ++sl) {
+                    const int n = issued > sl ? (issued - sl + NSLOT - 1) / NSLOT : 0;
+                    if (n > 0) mbar_drain(&C.full[sl], (n - 1) & 1);
+                }
             }
         }
     } else if (warp == 1) {
@@ -481,83 +425,81 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
             const uint32_t lo_ringMN = sdesc_sw128_lo(smem_u32(smem + G::OFF_RING), CHUNK_BYTES);
             const uint32_t lo_q = sdesc_sw128_lo(smem_u32(smem + G::OFF_Q), 16);
             const uint32_t lo_p = sdesc_sw128_lo(smem_u32(smem + G::OFF_P), 16);
-            constexpr uint32_t U_CHUNK = CHUNK_BYTES >> 4;
+            constexpr uint32_t U_CHUNK = CHUNK_BYTES >> 4, U_SLOT = SLOT_BYTES >> 4;
             constexpr uint32_t U_QCH = QCH_BYTES >> 4, U_P = P_BYTES >> 4;
-            RingPlace ring;
-            int n = 0;
+            int slot = 0, phase = 0;
             bool ok = true;
-            // wait for the next ring entry (nch chunks); returns its first chunk in the ring
-            auto take = [&](int nch) -> uint32_t {
-                const uint32_t start = ring.place(nch);
-                ok = ok && mbar_wait(&C.full[n % NBAR], (n / NBAR) & 1, abort_flag);
-                ++n;
-                return start % RING_CHUNKS;
+            auto take = [&]() -> uint32_t {   // wait for the next ring entry, return its slot
+                const uint32_t s_ = slot;
+                ok = ok && mbar_wait(&C.full[slot], phase, abort_flag);
+                if (++slot == NSLOT) {
+                    slot = 0;
+                    phase ^= 1;
+                }
+                return s_;
             };
-            auto release = [&]() { mma_commit(&C.empty[(n - 1) % NBAR]); };
             int g1 = 0, g2 = 0;
-            // K entry e of tile t (MMA1 into S[t & 1]); the first one of a segment's first tile
-            // waits for the segment's Q; the last one signals S
-            auto mma1_entry = [&](int t, int e) {
-                if (e == 0) {
-                    const Seg& sg = seg_of(t, g1);
-                    if (t == sg.first) ok = ok && mbar_wait(&C.q_full, g1 & 1, abort_flag);
-                }
+            // MMA1 of tile t into S[t & 1]; the first tile of segment g waits for its Q
+            // K entries [e0, e1) of tile t (MMA1 into S[t & 1]): the first waits for the Q of
+            // a segment's first tile, the last signals S
+            auto mma1 = [&](int t, int e0, int e1) {
+                if (e0 >= e1) return;
+                const Seg& sg = seg_of(t, g1);
+                if (e0 == 0 && t == sg.first) ok = ok && mbar_wait(&C.q_full, g1 & 1, abort_flag);
                 const uint32_t dS = tmem + TM_S + 32 * (t & 1);
-                const int c0 = K_GROUP * e, nch = min(K_GROUP, G::NCOL - c0);
-                const uint32_t at = take(nch);
-                if (!ok) return;
-                tc_fence_after();
-                for (int j = 0; j < nch; ++j) {
-                    const uint32_t a = lo_ringK + (at + j) * U_CHUNK;
-                    const uint32_t b = lo_q + (c0 + j) * U_QCH;
+                for (int e = e0; e < e1 && ok; ++e) {
+                    const uint32_t sl = take();
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t a = lo_ringK + sl * U_SLOT;
+                    const uint32_t b = lo_q + 2 * e * U_QCH;
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        mma_f16(dS, sdesc_join(a + 2 * kk, hi), sdesc_join(b + 2 * kk, hi),
-                                idesc_s, (c0 + j + kk) != 0 ? 1u : 0u);
+                    for (int hf = 0; hf < 2; ++hf) {
+                        if (hf == 1 && e == G::LAT_PAIRS) break;
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            mma_f16(dS, sdesc_join(a + hf * U_CHUNK + 2 * kk, hi),
+                                    sdesc_join(b + hf * U_QCH + 2 * kk, hi), idesc_s,
+                                    (e | hf | kk) != 0 ? 1u : 0u);
+                    }
+                    mma_commit(&C.empty[sl]);
                 }
-                release();
-                if (e == G::K_ENTRIES - 1) mma_commit(&C.s_full[t & 1]);
+                if (ok && e1 == G::K_ENTRIES) mma_commit(&C.s_full[t & 1]);
             };
-            // V entry e of tile i (MMA2 into the O^T blocks it covers); the first one waits for
-            // P(i); the first tile of a segment starts a fresh accumulator
-            auto mma2_entry = [&](int i, int e, bool first) {
+            // V entries [b0, b1) of tile i (MMA2 into those latent blocks): the first needs P(i);
+            // the first tile of a segment starts a fresh accumulator; the last signals o_done
+            auto mma2 = [&](int i, int b0, int b1) {
+                if (b0 >= b1 || !ok) return;
                 const Seg& sg = seg_of(i, g2);
-                if (first) {
-                    ok = ok && mbar_wait(&C.p_full[i & 1], (i >> 1) & 1, abort_flag);
+                if (b0 == 0) {
+                    ok = mbar_wait(&C.p_full[i & 1], (i >> 1) & 1, abort_flag);
                     if (!ok) return;
                     tc_fence_after();
                 }
-                const uint32_t b0 = lo_p + (i & 1) * U_P;
+                const uint32_t p0 = lo_p + (i & 1) * U_P;
                 const uint32_t acc0 = i != sg.first ? 1u : 0u;
-                const int p0 = V_GROUP * e, np = min(V_GROUP, G::LAT_PAIRS - p0);
-                const uint32_t at = take(2 * np);
-                if (!ok) return;
-                tc_fence_after();
-                for (int j = 0; j < np; ++j) {
-                    const uint32_t a0 = lo_ringMN + (at + 2 * j) * U_CHUNK;
+                for (int b = b0; b < b1 && ok; ++b) {
+                    const uint32_t sl = take();
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t a0 = lo_ringMN + sl * U_SLOT;
 #pragma unroll
                     for (int ks = 0; ks < 8; ++ks)
-                        mma_f16(tmem + TM_O + 32 * (p0 + j), sdesc_join(a0 + ks * (2048 >> 4), hi),
-                                sdesc_join(b0 + (ks >> 2) * U_QCH + 2 * (ks & 3), hi), idesc_o,
+                        mma_f16(tmem + TM_O + 32 * b, sdesc_join(a0 + ks * (2048 >> 4), hi),
+                                sdesc_join(p0 + (ks >> 2) * U_QCH + 2 * (ks & 3), hi), idesc_o,
                                 ks > 0 ? 1u : acc0);
+                    mma_commit(&C.empty[sl]);
                 }
-                release();
+                if (ok && b1 == G::V_ENTRIES) mma_commit(&C.o_done);
             };
-            for (int e = 0; e < G::K_ENTRIES && ok && NT > 0; ++e) mma1_entry(0, e);
+            if (NT > 0) mma1(0, 0, G::K_ENTRIES);
             for (int i = 0; i < NT && ok; ++i) {
-                // period i: the schedule's mix of MMA1(i+1) and MMA2(i) entries
-                bool first_v = true;
-#pragma unroll
-                for (int j = 0; j < Sched<G>::N; ++j) {
-                    const int c = Sched<G>::at(j);
-                    if (c >= 0) {
-                        if (i + 1 < NT) mma1_entry(i + 1, c);
-                    } else {
-                        mma2_entry(i, -1 - c, first_v);
-                        first_v = false;
-                    }
-                }
-                if (ok) mma_commit(&C.o_done);
+                // period i in ring order: MMA1 of tile i + 1 and MMA2 of tile i
+                const bool more = i + 1 < NT;
+                if (more) mma1(i + 1, 0, G::K_SPLIT);
+                mma2(i, 0, G::V_SPLIT);
+                if (more) mma1(i + 1, G::K_SPLIT, G::K_ENTRIES);
+                mma2(i, G::V_SPLIT, G::V_ENTRIES);
             }
             mma_commit(&C.o_full);
         }

@@ -8,7 +8,9 @@
 #   - compiles the patched ggml-cuda.cu and the shim with nvcc for sm_100a (the backend's dispatch
 #     and supports_op hooks and the launchers, against ggml-cuda's own headers);
 #   - builds the patched ggml core + ggml-cpu with gcc/g++ and links m4b_ggml_check, which builds
-#     the M4 nodes through ggml's builders and asks libm4b's supports_op (tests/test_ggml_boundary.py).
+#     the M4 nodes through ggml's builders and asks libm4b's supports_op (tests/test_ggml_boundary.py);
+#   - compiles the engine's layer graph (engine/m1_layer.cpp) with m1-layer-batch.patch, which
+#     keeps the fused ops for token batches (KQKV over each row's window).
 # The reference's CMake is not run: the source lists and definitions below are this file's own.
 # Every output goes to $(OUT), which is git-ignored and not sent to the GPU box.
 #
@@ -40,7 +42,7 @@ CUDA_FLAGS := -std=c++17 -gencode arch=compute_100a,code=sm_100a -O2 -Xcompiler 
 
 OBJS := $(addprefix $(OUT)/obj/,$(addsuffix .o,$(BASE_C) $(BASE_CXX) $(CPU_C) $(CPU_CXX)))
 
-all: $(OUT)/m4b_ggml_check $(OUT)/cuda/ggml-cuda.o $(OUT)/cuda/m4-b200.o
+all: $(OUT)/m4b_ggml_check $(OUT)/cuda/ggml-cuda.o $(OUT)/cuda/m4-b200.o $(OUT)/engine/m1_layer.o
 
 $(OUT)/gen/ggml-version.h:
 	@mkdir -p $(dir $@)
@@ -81,5 +83,18 @@ $(OUT)/cuda/ggml-cuda.o: $(OUT)/.patched $(OUT)/gen/ggml-version.h
 $(OUT)/cuda/m4-b200.o: $(OUT)/.patched $(OUT)/gen/ggml-version.h include/m4b.h
 	@mkdir -p $(dir $@)
 	$(NVCC) $(CUDA_FLAGS) -c $(TREE)/src/ggml-cuda/m4-b200.cu -o $@
+
+# the engine's layer graph with m1-layer-batch.patch (the fused ops kept at nt > 1, KQKV over the
+# rows' windows), compiled against the patched ggml headers: the caller side of the ragged path
+ENGINE_SRC := m1_layer.cpp m1_layer.h gguf_model.h store.h
+$(OUT)/engine/.patched: $(HERE)/m1-layer-batch.patch
+	@test -d $(REF)/engine || { echo "reference engine not found under $(REF)"; exit 1; }
+	rm -rf $(OUT)/engine && mkdir -p $(OUT)/engine
+	cp $(addprefix $(REF)/engine/,$(ENGINE_SRC)) $(OUT)/engine/
+	patch -s -d $(OUT)/engine -p1 < $(HERE)/m1-layer-batch.patch
+	touch $@
+
+$(OUT)/engine/m1_layer.o: $(OUT)/engine/.patched $(OUT)/.patched
+	g++ -std=c++17 -O1 -c $(OUT)/engine/m1_layer.cpp -I$(TREE)/include -o $@
 
 .PHONY: all

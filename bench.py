@@ -618,8 +618,11 @@ def measure(w, args, rank: int, world: int, dev, sample_clocks: bool = True) -> 
     r = {"ms_per_step": ms_max / args.steps, "value": L * args.steps / (ms_max * 1e-3),
          "clocks": clocks}
 
-    # ---- end to end: host queries in, host outputs back, every step
-    q_host = torch.randn((args.steps,) + tuple(w.q.shape), pin_memory=True)
+    # ---- end to end: host queries in, host outputs back, every step (the same seeded queries on
+    # every rank: the ranks of one job share each token's query)
+    q_dev = w.q.clone()
+    q_host = torch.randn((args.steps,) + tuple(w.q.shape),
+                         generator=torch.Generator().manual_seed(1234), pin_memory=True)
     out_host = torch.empty((args.steps,) + tuple(w.out.shape), pin_memory=True)
     graph_e2e = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph_e2e):
@@ -666,6 +669,7 @@ def measure(w, args, rank: int, world: int, dev, sample_clocks: bool = True) -> 
     del graph, graph_e2e, graph_kq           # release graphs before the process group
 
     # ---- parity: one eager step, its last layer against a float64 evaluation (outside timing)
+    w.q.copy_(q_dev)
     w.step()
     torch.cuda.synchronize()
     assert m4.device_status() == m4.OK

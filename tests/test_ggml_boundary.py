@@ -10,7 +10,8 @@ ragged form, and ggml-cuda's supports_op asks libm4b.  aubier_b200/ggml/ggml.mk 
   * m4b_ggml_check, linked with the patched ggml core + ggml-cpu and libm4b, builds the nodes the
     engine builds (engine/m1_layer.cpp:415-502) through ggml's builders and runs libm4b's
     supports_op on them exactly as ggml-cuda does, before any memory exists;
-  * a graph with an M4 node computed on ggml-cpu aborts (ggml-cpu.c:2064-2082), in a subprocess.
+  * a graph with an M4 node computed on ggml-cpu aborts (ggml-cpu.c:2064-2082), in a subprocess;
+  * the engine's layer graph with m1-layer-batch.patch (fused ops kept for token batches) compiles.
 No GPU is involved: supports_op makes no CUDA call and the CPU backend never reaches libm4b.
 """
 import os
@@ -119,3 +120,16 @@ def test_ggml_cuda_dispatch_and_shims_compile_for_sm100(check):
         assert f"U {fn}" in backend, fn          # called by the backend's dispatch / supports_op
     for fn in ("m4b_wkb", "m4b_kqkv", "m4b_kqkv_ragged", "m4b_phase", "m4b_supports_op"):
         assert f"U {fn}" in shim, fn             # resolved by libm4b at link time
+
+
+def test_engine_layer_keeps_the_fused_ops_for_batches(check):
+    """m1-layer-batch.patch: engine/m1_layer.cpp's gate (m1_layer.cpp:283-297) keeps WKB, KQKV and
+    W_UV on for up to 64 tokens, and at nt > 1 builds KQKV with ggml_m4_kqkv_ragged over each row's
+    window (the cells its mask opens, m1_layer.cpp:756-773), staged as two I32 inputs.  The patched
+    file compiles against the patched ggml headers."""
+    obj = os.path.join(OUT, "engine", "m1_layer.o")
+    out = subprocess.run(["nm", "-C", obj], capture_output=True, text=True, check=True).stdout
+    used = {l.split()[-1] for l in out.splitlines() if l.strip().startswith("U ")}
+    for fn in ("ggml_m4_wkb", "ggml_m4_kqkv", "ggml_m4_kqkv_ragged", "ggml_m4_phase_wvb",
+               "ggml_m4_phase_kvwrite"):
+        assert fn in used, fn

@@ -96,3 +96,53 @@ def test_lost_rank_fails_the_exchange_instead_of_hanging(tmp_path):
             pytest.fail("a rank hung on a lost peer")
     with open(path) as f:
         assert f.read().startswith("error:")
+
+
+def _ragged_worker(rank, world, port, result_path):
+    """Config 5's sharding on gloo ranks: whole sequences per rank by LPT on key counts, each rank
+    packs its own sequences' caches back to back and runs every token over its window [base,
+    base + len) of that packed cache (the engine's batch mask, m1_layer.cpp:756-773; the batch rig's
+    per-sequence regions, tools/m1_batch_test.cpp:19-24), then rank 0 gathers the outputs."""
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "tests")]
+    from aubier_b200.shard import lpt_assign, packed_bases
+    from mla_inputs import BASELINE as G, make_layer
+    from oracle import oracle as O
+    _init(rank, world, port)
+    lengths = [300, 1000, 129, 2000, 50, 700, 1, 1500]
+    _, w_uk, _, w_uv = make_layer(95, 1)
+    mine = lpt_assign(lengths, world)[rank]
+    # sequence i's cache and query depend on i only, not on the rank that holds it
+    caches = {i: make_layer(200 + i, lengths[i])[2] for i in mine}
+    queries = {i: make_layer(200 + i, 1)[0] for i in mine}
+    packed = np.concatenate([caches[i] for i in mine]) if mine else None
+    bases = packed_bases([lengths[i] for i in mine])
+    outs = {}
+    for i, base in zip(mine, bases):
+        window = packed[base:base + lengths[i]]
+        _, _, _, out = O.mla_step(w_uk, queries[i], window, None, w_uv, G.scale, G.nope)
+        outs[i] = out
+    gathered = [None] * world
+    dist.all_gather_object(gathered, outs)
+    if rank == 0:
+        got = {}
+        for part in gathered:
+            for i, out in part.items():
+                assert i not in got, f"sequence {i} ran on two ranks"
+                got[i] = out
+        assert sorted(got) == list(range(len(lengths))), "a sequence ran nowhere"
+        single = [O.mla_step(w_uk, make_layer(200 + i, 1)[0], make_layer(200 + i, n)[2], None,
+                             w_uv, G.scale, G.nope)[3] for i, n in enumerate(lengths)]
+        np.save(result_path, np.stack([np.stack([got[i] for i in range(len(lengths))]),
+                                       np.stack(single)]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_ragged_batch_sharded_by_sequence_matches_single_rank(tmp_path, world):
+    path = str(tmp_path / "ragged.npy")
+    mp.spawn(_ragged_worker, args=(world, _free_port(), path), nprocs=world, join=True)
+    sharded, single = np.load(path)
+    assert np.array_equal(sharded, single)   # same per-token arithmetic, only the placement moved
