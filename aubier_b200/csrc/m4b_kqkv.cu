@@ -56,8 +56,18 @@ constexpr int SLOT_BYTES = 2 * CHUNK_BYTES;
 constexpr int NSLOT = 5;                // FIFO ring: 5 x 32 KB
 // 1: each period's ring order puts half of tile i's V pass between tile i + 1's latent pairs and
 // its rope chunk, so the HBM reads of the K pass are spread over the period (Geo::K_SPLIT).
+// Measured on one box: 71.7-71.9 us at 262,144 keys against 67.3-68.0 us in the plain order (and
+// 140 against 124-126 us for the config-5 batch), so it is off.
 #ifndef M4B_KQ_INTERLEAVE
 #define M4B_KQ_INTERLEAVE 0
+#endif
+// 1: every K pass and every V pass completes one barrier (each entry adds its bytes, the pass's
+// last entry arrives), so the MMA issuer tests one barrier per pass instead of one per entry;
+// slots are still released one entry at a time.  Measured on one box at 262,144 keys: 77.3-78.4 us
+// against 67.3-70.5 us with the per-entry waits (the issuer can no longer start a pass before all of
+// it has landed), so it is off.
+#ifndef M4B_KQ_PASS_WAIT
+#define M4B_KQ_PASS_WAIT 0
 #endif
 constexpr int QCH_BYTES = H * 128;      // 32 heads x 64 columns f16 = 4 KB
 constexpr int P_BYTES = 2 * QCH_BYTES;  // 32 heads x 128 keys f16 = 8 KB (double-buffered)
@@ -126,6 +136,7 @@ static_assert(sizeof(Seg) == 32, "segment table entry");
 struct Ctrl {
     uint64_t full[NSLOT];
     uint64_t empty[NSLOT];
+    uint64_t kpass[2], vpass[2];   // M4B_KQ_PASS_WAIT: tile t's K / V pass landed ([t & 1], phase t >> 1)
     uint64_t s_full[2], p_full[2];
     uint64_t q_full, o_done, o_full;
     uint64_t red_full[2];   // per head group, once per tile: the 4 warps' flags / maxima are in
@@ -280,6 +291,8 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
             mbar_init(&C.empty[i], 1);
         }
         for (int b = 0; b < 2; ++b) {
+            mbar_init(&C.kpass[b], 1);
+            mbar_init(&C.vpass[b], 1);
             mbar_init(&C.s_full[b], 1);
             mbar_init(&C.p_full[b], 8);
             mbar_init(&C.red_full[b], 4);
@@ -366,15 +379,26 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
             const uint64_t pol_keep = l2_policy_evict_last();    // K pass: V is re-read soon
             const uint64_t pol_done = l2_policy_evict_first();   // V pass: last use
             int slot = 0, phase = 0, issued = 0;
+            int kstarted = 0, kpasses = 0;  // K passes with an entry issued / with all issued
+            int vstarted = 0, vpasses = 0;
             bool ok = true;
-            // one ring entry: chunks c0 (and c0 + 1 when two) of the tile at cache row key0
-            auto entry = [&](int key0, int c0, int two, uint64_t pol) {
+            // one ring entry: chunks c0 (and c0 + 1 when two) of the tile at cache row key0; with
+            // pass barriers, `pass` collects the pass's bytes and `last` ends its phase
+            auto entry = [&](int key0, int c0, int two, uint64_t pol, uint64_t* pass, bool last) {
                 ok = ok && mbar_wait(&C.empty[slot], phase ^ 1, abort_flag);
                 if (!ok) return;
-                mbar_arrive_expect_tx(&C.full[slot], two ? SLOT_BYTES : CHUNK_BYTES);
+                const uint32_t bytes = two ? SLOT_BYTES : CHUNK_BYTES;
+                uint64_t* bar = &C.full[slot];
+                if (M4B_KQ_PASS_WAIT) {
+                    bar = pass;
+                    if (last) mbar_arrive_expect_tx(bar, bytes);
+                    else mbar_expect_tx(bar, bytes);
+                } else {
+                    mbar_arrive_expect_tx(bar, bytes);
+                }
                 uint8_t* dst = smem + G::OFF_RING + slot * SLOT_BYTES;
-                tma_load_2d(dst, &tmap, 64 * c0, key0, &C.full[slot], pol);
-                if (two) tma_load_2d(dst + CHUNK_BYTES, &tmap, 64 * (c0 + 1), key0, &C.full[slot], pol);
+                tma_load_2d(dst, &tmap, 64 * c0, key0, bar, pol);
+                if (two) tma_load_2d(dst + CHUNK_BYTES, &tmap, 64 * (c0 + 1), key0, bar, pol);
                 ++issued;
                 if (++slot == NSLOT) {
                     slot = 0;
@@ -394,12 +418,21 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
                     vkey = sg.row0 + (t - sg.first) * TK;
                 }
                 auto kpart = [&](int e0, int e1) {
-                    if (kkey >= 0)
-                        for (int e = e0; e < e1; ++e) entry(kkey, 2 * e, e < G::LAT_PAIRS, pol_keep);
+                    if (kkey < 0) return;
+                    for (int e = e0; e < e1 && ok; ++e) {
+                        entry(kkey, 2 * e, e < G::LAT_PAIRS, pol_keep, &C.kpass[(t + 1) & 1],
+                              e == G::K_ENTRIES - 1);
+                        if (ok && e == 0) ++kstarted;
+                        if (ok && e == G::K_ENTRIES - 1) ++kpasses;
+                    }
                 };
                 auto vpart = [&](int e0, int e1) {
-                    if (vkey >= 0)
-                        for (int e = e0; e < e1; ++e) entry(vkey, 2 * e, 1, pol_done);
+                    if (vkey < 0) return;
+                    for (int e = e0; e < e1 && ok; ++e) {
+                        entry(vkey, 2 * e, 1, pol_done, &C.vpass[t & 1], e == G::V_ENTRIES - 1);
+                        if (ok && e == 0) ++vstarted;
+                        if (ok && e == G::V_ENTRIES - 1) ++vpasses;
+                    }
                 };
                 kpart(0, G::K_SPLIT);
                 vpart(0, G::V_SPLIT);
@@ -408,9 +441,20 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
             }
             if (*abort_flag) {
                 // let this CTA's own copies land before its shared memory is released
-                for (int sl = 0; sl < NSLOT; ++sl) {
-                    const int n = issued > sl ? (issued - sl + NSLOT - 1) / NSLOT : 0;
-                    if (n > 0) mbar_drain(&C.full[sl], (n - 1) & 1);
+                if (M4B_KQ_PASS_WAIT) {
+                    // a pass cut short gets its missing arrive, so its phase ends once the bytes
+                    // already requested have landed; then the last two passes of each kind
+                    if (kstarted > kpasses) mbar_arrive(&C.kpass[kpasses & 1]);
+                    if (vstarted > vpasses) mbar_arrive(&C.vpass[vpasses & 1]);
+                    for (int x = kstarted > 2 ? kstarted - 2 : 0; x < kstarted; ++x)
+                        mbar_drain(&C.kpass[x & 1], (x >> 1) & 1);
+                    for (int x = vstarted > 2 ? vstarted - 2 : 0; x < vstarted; ++x)
+                        mbar_drain(&C.vpass[x & 1], (x >> 1) & 1);
+                } else {
+                    for (int sl = 0; sl < NSLOT; ++sl) {
+                        const int n = issued > sl ? (issued - sl + NSLOT - 1) / NSLOT : 0;
+                        if (n > 0) mbar_drain(&C.full[sl], (n - 1) & 1);
+                    }
                 }
             }
         }
@@ -431,7 +475,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
             bool ok = true;
             auto take = [&]() -> uint32_t {   // wait for the next ring entry, return its slot
                 const uint32_t s_ = slot;
-                ok = ok && mbar_wait(&C.full[slot], phase, abort_flag);
+                if (!M4B_KQ_PASS_WAIT) ok = ok && mbar_wait(&C.full[slot], phase, abort_flag);
                 if (++slot == NSLOT) {
                     slot = 0;
                     phase ^= 1;
@@ -446,11 +490,16 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
                 if (e0 >= e1) return;
                 const Seg& sg = seg_of(t, g1);
                 if (e0 == 0 && t == sg.first) ok = ok && mbar_wait(&C.q_full, g1 & 1, abort_flag);
+                if (M4B_KQ_PASS_WAIT && e0 == 0) {   // the whole K pass of tile t has landed
+                    ok = ok && mbar_wait(&C.kpass[t & 1], (t >> 1) & 1, abort_flag);
+                    if (!ok) return;
+                    tc_fence_after();
+                }
                 const uint32_t dS = tmem + TM_S + 32 * (t & 1);
                 for (int e = e0; e < e1 && ok; ++e) {
                     const uint32_t sl = take();
                     if (!ok) break;
-                    tc_fence_after();
+                    if (!M4B_KQ_PASS_WAIT) tc_fence_after();
                     const uint32_t a = lo_ringK + sl * U_SLOT;
                     const uint32_t b = lo_q + 2 * e * U_QCH;
 #pragma unroll
@@ -473,6 +522,8 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
                 const Seg& sg = seg_of(i, g2);
                 if (b0 == 0) {
                     ok = mbar_wait(&C.p_full[i & 1], (i >> 1) & 1, abort_flag);
+                    if (M4B_KQ_PASS_WAIT)   // the whole V pass of tile i has landed
+                        ok = ok && mbar_wait(&C.vpass[i & 1], (i >> 1) & 1, abort_flag);
                     if (!ok) return;
                     tc_fence_after();
                 }
@@ -481,7 +532,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
                 for (int b = b0; b < b1 && ok; ++b) {
                     const uint32_t sl = take();
                     if (!ok) break;
-                    tc_fence_after();
+                    if (!M4B_KQ_PASS_WAIT) tc_fence_after();
                     const uint32_t a0 = lo_ringMN + sl * U_SLOT;
 #pragma unroll
                     for (int ks = 0; ks < 8; ++ks)
