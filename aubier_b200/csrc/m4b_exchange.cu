@@ -235,7 +235,7 @@ __global__ void __cluster_dims__(1, kLatent / 128, 1) __launch_bounds__(THREADS)
 merge_exchange_wvb_kernel(const float* __restrict__ part, int S, PeerPtrs peers, char* local,
                           int world, int rank, Layout L, const __half* __restrict__ w_uv,
                           float* __restrict__ attn_out, int64_t attn_hs, float* __restrict__ out,
-                          int64_t out_hs) {
+                          int64_t out_hs, int release) {
     namespace cg = cooperative_groups;
     extern __shared__ float s_ml[];   // [2][S]
     __shared__ __align__(16) float s_red[THREADS / 32][128];
@@ -254,6 +254,7 @@ merge_exchange_wvb_kernel(const float* __restrict__ part, int S, PeerPtrs peers,
         const int j = 16 * warp + 2 * k + hw;
         wv[k] = kq::ldg_nc_u4(w_uv + (static_cast<size_t>(h) * kVHead + j) * kLatent + d0 + 8 * l16);
     }
+    if (release) pdl_launch_dependents();   // M4B_FLAG_EARLY_RELEASE: the next layer's loads may start
     pdl_wait();
     const uint64_t e = *reinterpret_cast<volatile uint64_t*>(local + L.epoch_off) + 1;
     const uint32_t e32 = static_cast<uint32_t>(e);
@@ -544,7 +545,8 @@ M4B_API int m4b_exchange_merge_wvb(m4b_exchange* x, const m4b_phase_args* a,
                             x->world, x->rank, xch::layout(x->world),
                             static_cast<const __half*>(a->src[0].data), attn, attn_hs,
                             static_cast<float*>(a->dst.data),
-                            static_cast<int64_t>(a->dst.nb[2] / 4)));
+                            static_cast<int64_t>(a->dst.nb[2] / 4),
+                            (a->flags & M4B_FLAG_EARLY_RELEASE) ? 1 : 0));
 }
 
 }  // extern "C"

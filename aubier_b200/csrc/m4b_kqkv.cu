@@ -985,7 +985,7 @@ template <int R>
 __global__ void __cluster_dims__(1, R / 128, 1) __launch_bounds__(CMB_THREADS)
 kqkv_combine_wvb_kernel(const float* __restrict__ part, int S, const __half* __restrict__ w_uv,
                         float* __restrict__ attn_out, int64_t attn_hs, float* __restrict__ out,
-                        int64_t out_hs) {
+                        int64_t out_hs, int release) {
     namespace cg = cooperative_groups;
     extern __shared__ float s_ml[];   // [2][S]: m then alpha, l
     __shared__ __align__(16) float s_red[CMB_THREADS / 32][128];
@@ -1006,6 +1006,7 @@ kqkv_combine_wvb_kernel(const float* __restrict__ part, int S, const __half* __r
         const int j = 16 * warp + 2 * k + hw;
         wv[k] = ldg_nc_u4(w_uv + (static_cast<size_t>(h) * kVHead + j) * R + d0 + 8 * l16);
     }
+    if (release) pdl_launch_dependents();   // M4B_FLAG_EARLY_RELEASE: the next layer's loads may start
     pdl_wait();
 
     float mstar, l, o;
@@ -1179,7 +1180,8 @@ cudaError_t launch_kqkv_combine_wvb(const float* part, int S, const void* w_uv, 
     if (smem > 48 * 1024) return note(cudaErrorInvalidValue);
     return launch(kq::kqkv_combine_wvb_kernel<kLatent>, dim3(kHeads, kLatent / 128),
                   dim3(kq::CMB_THREADS), smem, stream, flags, part, S,
-                  static_cast<const __half*>(w_uv), attn_out, attn_hs, out, out_hs);
+                  static_cast<const __half*>(w_uv), attn_out, attn_hs, out, out_hs,
+                  (flags & M4B_FLAG_EARLY_RELEASE) ? 1 : 0);
 }
 
 cudaError_t launch_kqkv_ragged_combine(const float* part, const int32_t* seq_base,

@@ -37,7 +37,7 @@ PART_STRIDE = LATENT + 4   # o[512], m (log2 units), l, 2 pad
 TILE_KEYS = 128            # keys per KQKV tile: splits are balanced over ceil(N / 128) tiles
 
 F32, F16, Q8_0, I32, I64 = 0, 1, 8, 26, 27
-FLAG_PDL, FLAG_KV_STATIC, FLAG_QCAT = 1, 2, 4
+FLAG_PDL, FLAG_KV_STATIC, FLAG_QCAT, FLAG_EARLY_RELEASE = 1, 2, 4, 8
 OK, EINVAL, ESCRATCH, ECUDA, EDEVICE, ENOTSUP, ETIMEOUT = range(7)
 
 OP_WKB, OP_KQKV, OP_PHASE = 0, 1, 2

@@ -275,6 +275,8 @@ def slab_workload(args, rank, world, dev):
         torch.cuda.synchronize()            # every rank's inputs exist before the first exchange
         dist.barrier()
     flags = m4.FLAG_PDL
+    # short slabs: the merge releases the next layer's launch once its W_UV loads are issued
+    early = m4.FLAG_EARLY_RELEASE if n_loc <= 65536 else 0
 
     def step():
         for layer in range(L):
@@ -283,12 +285,13 @@ def slab_workload(args, rank, world, dev):
             m4.kqkv_partials(kc[layer], qcur[layer], mask[layer], SCALE, out=part,
                              flags=flags | m4.FLAG_KV_STATIC)
             if xchg is not None:   # one launch: merge, NVLink stores into every peer, wait, merge, W_UV
-                xchg.merge_wvb(part, wuv[layer], out=w.out[layer], attn_out=attn, flags=flags)
+                xchg.merge_wvb(part, wuv[layer], out=w.out[layer], attn_out=attn, flags=flags | early)
                 continue
             if world > 1:   # library collective: merge the local splits, all-gather 66 KB per rank
                 m4.phase_merge_records(part, out=merged, flags=flags)
                 dist.all_gather_into_tensor(gathered, merged)
-            m4.phase_combine_wvb(wuv[layer], gathered, out=w.out[layer], attn_out=attn, flags=flags)
+            m4.phase_combine_wvb(wuv[layer], gathered, out=w.out[layer], attn_out=attn,
+                                 flags=flags | early)
 
     def kq():
         for layer in range(L):
@@ -339,7 +342,8 @@ def slab_workload(args, rank, world, dev):
                 "l2": f"inputs larger than L2 ({L} layers x {1156 * N / 1e6:.1f} MB KV + mask "
                       "per step)",
                 "step": "WKB -> KQKV split-K partials -> PHASE combine+W_UV per layer, "
-                        "one CUDA graph per step"}
+                        "one CUDA graph per step",
+                "early_release": bool(early)}
     w.close = (lambda: xchg.close()) if xchg is not None else (lambda: None)
     w.lengths = [N]
     return w

@@ -91,7 +91,14 @@ enum m4b_flags {
        q_nope in src1's head row -- into dst's head row right after the latent, so dst holds the
        graph's Qcur = concat(q_abs, q_pe) (engine/m1_layer.cpp:443-447) without a separate copy.
        Needs src1's head stride >= nope + 64 floats and dst's >= latent + 64 floats. */
-    M4B_FLAG_QCAT      = 1u << 2
+    M4B_FLAG_QCAT      = 1u << 2,
+    /* with M4B_FLAG_PDL on PHASE selector 2 and m4b_exchange_merge_wvb: release the next kernel
+       of the stream as soon as this one's W_UV loads are issued, instead of at completion, so the
+       next layer's weight loads overlap this merge.  The next kernel still waits for this one's
+       results.  Worth it when a layer's slab is short (measured: 5 % faster layer-steps at 32,768
+       keys); at 262,144 keys the early start competes for HBM and is slower.  Other entry points
+       ignore it. */
+    M4B_FLAG_EARLY_RELEASE = 1u << 3
 };
 
 /*

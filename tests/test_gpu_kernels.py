@@ -388,3 +388,46 @@ def test_contract_violations_raise(m4):
     assert e.value.code == m4.ESCRATCH
     with pytest.raises(m4.M4Error):
         m4.kqkv(kc.cpu(), q.cpu(), None, SCALE)              # no CPU handler
+
+
+def test_early_release_chain_is_bit_identical(m4):
+    """M4B_FLAG_EARLY_RELEASE only moves the point at which the next launch may start: a chain of
+    layers (WKB -> KQKV partials -> merge + W_UV) replayed from a CUDA graph gives the same bits
+    with and without it, and each layer still matches the oracle.  (Set on KQKV as well, it is
+    ignored there: releasing the cluster-launched merge from KQKV early made the merge read the
+    records too soon in graph replay.)"""
+    import torch
+    L, N = 4, 5000
+    layers = [make_layer(600 + l, N) for l in range(L)]
+    d = [tuple(dev(a) for a in lay) for lay in layers]
+    S = m4.default_splits(N)
+
+    def run(extra):
+        part = torch.empty(S, G.H, G.R + 4, device="cuda")
+        outs = torch.empty(L, G.H, G.V, device="cuda")
+        qcur = [torch.empty(G.H, G.D, device="cuda") for _ in range(L)]
+
+        def chain():
+            for l, (q, w_uk, kc, w_uv) in enumerate(d):
+                m4.wkb(w_uk, q[:, :G.nope], out=qcur[l][:, :G.R], flags=m4.FLAG_PDL | m4.FLAG_QCAT)
+                m4.kqkv_partials(kc, qcur[l], None, SCALE, out=part,
+                                 flags=m4.FLAG_PDL | m4.FLAG_KV_STATIC | extra)   # ignored
+                m4.phase_combine_wvb(w_uv, part, out=outs[l], flags=m4.FLAG_PDL | extra)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            chain()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            chain()
+        for _ in range(3):
+            g.replay()
+        return host(outs)
+
+    plain, early = run(0), run(m4.FLAG_EARLY_RELEASE)
+    assert m4.device_status() == m4.OK
+    assert np.array_equal(plain, early)
+    for l, (q, w_uk, kc, w_uv) in enumerate(layers):
+        _, _, _, ref = O.mla_step(w_uk, q, kc, None, w_uv, SCALE, G.nope)
+        assert rel_to_max(early[l], ref) <= ATTN_TOL
