@@ -579,7 +579,7 @@ int m4b_phase(const m4b_phase_args* a, m4b_stream_t stream) {
         return status_of(launch_kqkv_combine_wvb(
             static_cast<const float*>(a->src[1].data), n_rec, a->src[0].data,
             a->src[2].data != nullptr ? attn : nullptr, attn_hs, out, out_hs,
-            a->flags & M4B_FLAG_PDL, s));
+            a->flags & (M4B_FLAG_PDL | M4B_FLAG_EARLY_RELEASE), s));
     cudaError_t e = launch_kqkv_combine(static_cast<const float*>(a->src[1].data),
                                         static_cast<int>(a->src[1].ne[2]), kGeo[geom].latent, attn,
                                         attn_hs, a->flags & M4B_FLAG_PDL, s);

@@ -276,7 +276,7 @@ def slab_workload(args, rank, world, dev):
         dist.barrier()
     flags = m4.FLAG_PDL
     # short slabs: the merge releases the next layer's launch once its W_UV loads are issued
-    early = m4.FLAG_EARLY_RELEASE if n_loc <= 65536 else 0
+    early = m4.FLAG_EARLY_RELEASE if n_loc <= 131072 else 0
 
     def step():
         for layer in range(L):
