@@ -69,19 +69,32 @@ __device__ __forceinline__ void st_word(uint64_t* a, float v, uint32_t e) {
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(w) : "memory");
 }
 
-// Poll one word until it carries epoch e; bounded: after g_wait_limit cycles (counted from t0)
-// the device status becomes TIMEOUT and whatever the word holds is returned.
-__device__ __forceinline__ float ld_word(const uint64_t* a, uint32_t e, long long t0) {
-    uint64_t w;
+// Poll N words at once until each carries epoch e: every pending word's load is in flight
+// together, so once the records are in, the wait costs one L2 round trip instead of one per word
+// (per rank).  Bounded: after g_wait_limit cycles (counted from t0) the device status becomes
+// TIMEOUT and whatever the words hold is returned.  Words outside `pending` are not read.
+template <int N>
+__device__ __forceinline__ void ld_words(const uint64_t* const (&a)[N], unsigned pending,
+                                         uint32_t e, long long t0, float (&v)[N]) {
+    uint64_t w[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k) w[k] = 0;
     for (;;) {
-        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(a) : "memory");
-        if (static_cast<uint32_t>(w >> 32) == e) break;
+#pragma unroll
+        for (int k = 0; k < N; ++k)
+            if ((pending >> k) & 1u)
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w[k]) : "l"(a[k]) : "memory");
+#pragma unroll
+        for (int k = 0; k < N; ++k)
+            if (((pending >> k) & 1u) && static_cast<uint32_t>(w[k] >> 32) == e) pending &= ~(1u << k);
+        if (pending == 0) break;
         if (wait_expired(t0)) {
             atomicExch(&g_status, DEV_STATUS_TIMEOUT);
             break;
         }
     }
-    return __uint_as_float(static_cast<uint32_t>(w));
+#pragma unroll
+    for (int k = 0; k < N; ++k) v[k] = __uint_as_float(static_cast<uint32_t>(w[k]));
 }
 
 constexpr int THREADS = 256;
@@ -162,19 +175,23 @@ gather_wvb_kernel(char* __restrict__ local, int world, Layout L, const __half* _
     const uint64_t e = *reinterpret_cast<volatile uint64_t*>(local + L.epoch_off);
     const uint32_t e32 = static_cast<uint32_t>(e);
     const long long t0 = clock64();
+    const unsigned all = (1u << world) - 1u;
     if (tid < world) {
         const uint64_t* rec = record(local, L, e, world, tid, h);
-        s_m[tid] = ld_word(rec + kPartM, e32, t0);
-        s_l[tid] = ld_word(rec + kPartL, e32, t0);
+        const uint64_t* a[2] = {rec + kPartM, rec + kPartL};
+        float ml[2];
+        ld_words<2>(a, 3u, e32, t0, ml);
+        s_m[tid] = ml[0];
+        s_l[tid] = ml[1];
     }
     float v[2][kMaxWorld];
 #pragma unroll
-    for (int r = 0; r < kMaxWorld; ++r) {
-        if (r < world) {
-            const uint64_t* rec = record(local, L, e, world, r, h);
-            v[0][r] = ld_word(rec + tid, e32, t0);
-            v[1][r] = ld_word(rec + tid + THREADS, e32, t0);
-        }
+    for (int c = 0; c < 2; ++c) {
+        const uint64_t* a[kMaxWorld];
+#pragma unroll
+        for (int r = 0; r < kMaxWorld; ++r)
+            a[r] = record(local, L, e, world, r < world ? r : 0, h) + tid + c * THREADS;
+        ld_words<kMaxWorld>(a, all, e32, t0, v[c]);
     }
     __syncthreads();
     float mstar = -INFINITY;
@@ -281,16 +298,20 @@ merge_exchange_wvb_kernel(const float* __restrict__ part, int S, PeerPtrs peers,
 
     // 2. every GPU's block of this exchange (bounded polls of the epoch in each word)
     const long long t0 = clock64();
-    if (tid < world) {
-        const uint64_t* rec = record(local, L, e, world, tid, h);
-        s_wm[tid] = ld_word(rec + kPartM, e32, t0);
-        s_wl[tid] = ld_word(rec + kPartL, e32, t0);
-    }
     float v[kMaxWorld];
-    if (tid < 128) {
+    if (tid < 128) {   // column d0 + tid of every rank's record, all polled together
+        const uint64_t* a[kMaxWorld];
 #pragma unroll
         for (int r = 0; r < kMaxWorld; ++r)
-            if (r < world) v[r] = ld_word(record(local, L, e, world, r, h) + d0 + tid, e32, t0);
+            a[r] = record(local, L, e, world, r < world ? r : 0, h) + d0 + tid;
+        ld_words<kMaxWorld>(a, (1u << world) - 1u, e32, t0, v);
+    } else if (tid - 128 < world) {   // m and l of rank tid - 128
+        const uint64_t* rec = record(local, L, e, world, tid - 128, h);
+        const uint64_t* a[2] = {rec + kPartM, rec + kPartL};
+        float ml[2];
+        ld_words<2>(a, 3u, e32, t0, ml);
+        s_wm[tid - 128] = ml[0];
+        s_wl[tid - 128] = ml[1];
     }
     __syncthreads();
     if (tid < 128) {
