@@ -5,6 +5,8 @@
   combine.  No kernel waits for another (every record is in place before any combine starts), and
   the result matches the oracle over the whole cache, in three consecutive exchanges so both
   halves of the double-buffered receive area are used.
+* The one-launch form (m4b_exchange_merge_wvb) as rank 0 of 2 and 8 ranks: the other ranks
+  publish first, so rank 0's polls find every record in place; matches the oracle.
 * Rank 1 never publishes: rank 0's one-launch exchange (m4b_exchange_merge_wvb) stores its record,
   then polls for rank 1's, which never comes.  With the wait limit shortened to a few milliseconds
   the kernel gives up, returns and reports M4B_ETIMEOUT through m4b_device_status(); the context
@@ -104,6 +106,41 @@ def test_in_process_exchange_on_one_gpu_matches_oracle(m4):
             _, _, attn_ref, out_ref = O.mla_step(w_uk, q, kc, None, w_uv, G.scale, G.nope)
             assert rel_to_max(attns[0].cpu().numpy(), attn_ref) <= ATTN_TOL
             assert rel_to_max(o0, out_ref) <= ATTN_TOL
+    finally:
+        _close(m4, hs)
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_one_launch_exchange_in_process_matches_oracle(m4, world):
+    """m4b_exchange_merge_wvb (merge, store into every rank's buffer, poll, merge, W_UV in one
+    launch) as rank 0 of `world` ranks in this process: ranks 1.. publish first (plain launches
+    that wait for nothing), so rank 0's polls find every record already in place and no kernel
+    waits for a later one.  Slabs of 19,000 keys give every rank the full 148 split records.
+    Three consecutive exchanges use both halves of the receive area."""
+    from oracle import oracle as O
+    lib = m4.lib()
+    slab = 19000
+    N = world * slab
+    hs = _local_exchange(m4, world)
+    try:
+        for k in range(3):
+            q, w_uk, kc, w_uv, qcur = _layer(130 + 7 * world + k, N)
+            kcd, qd, wuvd = (torch.from_numpy(a).cuda() for a in (kc, qcur, w_uv))
+            parts = [m4.kqkv_partials(kcd[r * slab:(r + 1) * slab], qd, None, G.scale)
+                     for r in range(world)]
+            for r in range(1, world):
+                rc = lib.m4b_exchange_publish(hs[r], ctypes.byref(_args(m4, part=parts[r])),
+                                              m4._stream())
+                assert rc == m4.OK, m4.strerror(rc)
+            out = torch.full((G.H, G.V), float("nan"), device="cuda")
+            attn = torch.full((G.H, G.R), float("nan"), device="cuda")
+            a = _args(m4, part=parts[0], w_uv=wuvd, out=out, attn=attn)
+            rc = lib.m4b_exchange_merge_wvb(hs[0], ctypes.byref(a), m4._stream())
+            assert rc == m4.OK, m4.strerror(rc)
+            assert m4.device_status() == m4.OK
+            _, _, attn_ref, out_ref = O.mla_step(w_uk, q, kc, None, w_uv, G.scale, G.nope)
+            assert rel_to_max(attn.cpu().numpy(), attn_ref) <= ATTN_TOL
+            assert rel_to_max(out.cpu().numpy(), out_ref) <= ATTN_TOL
     finally:
         _close(m4, hs)
 
