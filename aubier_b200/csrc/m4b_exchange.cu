@@ -14,10 +14,12 @@
 //
 // Per-GPU buffer (allocated once at set-up, shared by IPC handle):
 //   recv[2][world][32][516] u64   records {value, epoch}, double-buffered by epoch parity
-//   epoch u64                     exchanges published by this GPU so far
-//   arrive u32                    CTA arrival counter of the publishing kernel
-// Every value that changes per call (the epoch, the buffer parity) is read from device memory, so
-// both kernels can be captured once in a CUDA graph and replayed.
+//   epoch[32][4] u64              exchanges published so far, one count per (head, 128-column
+//                                 block): the CTA that publishes a block reads its count at the
+//                                 start and stores the next one at its end, so no CTA waits on
+//                                 another's bookkeeping (all counts move in step)
+// Every value that changes per call (the epochs, the buffer parity) is read from device memory, so
+// the kernels can be captured once in a CUDA graph and replayed.
 //
 // Reuse of a parity half is safe: a GPU publishes epoch e+2 only after its own consumer of epoch
 // e+1 saw every peer's e+1 record, which every peer published after consuming epoch e.
@@ -41,17 +43,25 @@ namespace xch {
 
 constexpr size_t kRecordWords = static_cast<size_t>(kHeads) * kPartStride;
 
+constexpr int kColBlocks = kLatent / 128;   // 128-column blocks per head record
+
 struct Layout {
-    size_t recv_off, epoch_off, arrive_off, bytes;
+    size_t recv_off, epoch_off, bytes;
 };
 
 inline Layout layout(int world) {
     Layout l;
     l.recv_off = 0;
     l.epoch_off = 2 * static_cast<size_t>(world) * kRecordWords * sizeof(uint64_t);
-    l.arrive_off = l.epoch_off + sizeof(uint64_t);
-    l.bytes = (l.arrive_off + 256 + 255) & ~static_cast<size_t>(255);
+    l.bytes = (l.epoch_off + kHeads * kColBlocks * sizeof(uint64_t) + 255) &
+              ~static_cast<size_t>(255);
     return l;
+}
+
+// the exchange count of head h's column block y on this GPU
+__device__ __forceinline__ volatile uint64_t* epoch_word(char* local, const Layout& L, int h,
+                                                         int y) {
+    return reinterpret_cast<volatile uint64_t*>(local + L.epoch_off) + h * kColBlocks + y;
 }
 
 struct PeerPtrs {
@@ -115,7 +125,8 @@ publish_kernel(const float* __restrict__ part, int S, PeerPtrs peers, char* loca
     const int tid = threadIdx.x;
     const size_t ss = static_cast<size_t>(kHeads) * kPartStride;
     const float* ph = part + static_cast<size_t>(h) * kPartStride;
-    const uint64_t e = *reinterpret_cast<volatile uint64_t*>(local + L.epoch_off) + 1;
+    volatile uint64_t* ep = epoch_word(local, L, h, blockIdx.y);
+    const uint64_t e = *ep + 1;
     float mstar, l, o;
     kq::merge_block_inflight<kLatent>(ph, S, ss, d0, s_ml, s_red, s_m, s_l, mstar, l, o);
     const uint32_t e32 = static_cast<uint32_t>(e);
@@ -131,16 +142,9 @@ publish_kernel(const float* __restrict__ part, int S, PeerPtrs peers, char* loca
             }
         }
     }
-    // The epoch advances once every CTA has read it (local bookkeeping; the next kernels on this
-    // GPU are ordered after this one by the stream).
-    __syncthreads();
-    if (tid == 0) {
-        unsigned* arrive = reinterpret_cast<unsigned*>(local + L.arrive_off);
-        if (atomicAdd(arrive, 1u) == gridDim.x * gridDim.y - 1) {
-            *arrive = 0;
-            *reinterpret_cast<volatile uint64_t*>(local + L.epoch_off) = e;
-        }
-    }
+    // this block's count advances (every thread read it before merge_block_inflight's first
+    // barrier; the next kernels on this GPU are ordered after this one by the stream)
+    if (tid == 0) *ep = e;
 }
 
 // Wait for every rank's record of head h (polling the epoch in each word), merge the `world`
@@ -172,7 +176,7 @@ gather_wvb_kernel(char* __restrict__ local, int world, Layout L, const __half* _
                                                  warp * GW_ROWS_PER_WARP + it) * kLatent +
                                          256 * u + 8 * lane);
     pdl_wait();
-    const uint64_t e = *reinterpret_cast<volatile uint64_t*>(local + L.epoch_off);
+    const uint64_t e = *epoch_word(local, L, h, 0);   // advanced by the publish just before
     const uint32_t e32 = static_cast<uint32_t>(e);
     const long long t0 = clock64();
     const unsigned all = (1u << world) - 1u;
@@ -273,7 +277,8 @@ merge_exchange_wvb_kernel(const float* __restrict__ part, int S, PeerPtrs peers,
     }
     if (release) pdl_launch_dependents();   // M4B_FLAG_EARLY_RELEASE: the next layer's loads may start
     pdl_wait();
-    const uint64_t e = *reinterpret_cast<volatile uint64_t*>(local + L.epoch_off) + 1;
+    volatile uint64_t* ep = epoch_word(local, L, h, blockIdx.y);
+    const uint64_t e = *ep + 1;
     const uint32_t e32 = static_cast<uint32_t>(e);
 
     // 1. this GPU's record block, stored into every GPU's slot [rank]
@@ -371,14 +376,8 @@ merge_exchange_wvb_kernel(const float* __restrict__ part, int S, PeerPtrs peers,
     }
     cluster.sync();
 
-    // 4. the epoch advances once every block has read it
-    if (tid == 0) {
-        unsigned* arrive = reinterpret_cast<unsigned*>(local + L.arrive_off);
-        if (atomicAdd(arrive, 1u) == gridDim.x * gridDim.y - 1) {
-            *arrive = 0;
-            *reinterpret_cast<volatile uint64_t*>(local + L.epoch_off) = e;
-        }
-    }
+    // 4. this block's count advances (read by every thread before the first barrier)
+    if (tid == 0) *ep = e;
 }
 
 }  // namespace xch
