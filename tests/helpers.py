@@ -21,7 +21,8 @@ def rel_to_max(x, ref) -> float:
 
 
 def elementwise_ok(x, ref, rtol=2e-3, atol_frac=1e-5) -> bool:
-    """|x - ref| <= rtol*|ref| + atol_frac*max|ref| everywhere (the survey's secondary check)."""
+    """|x - ref| <= rtol*|ref| + atol_frac*max|ref| everywhere (an elementwise check beside the
+    rel-to-max one)."""
     x = np.asarray(x, np.float64)
     ref = np.asarray(ref, np.float64)
     return bool(np.all(np.abs(x - ref) <= rtol * np.abs(ref) + atol_frac * np.abs(ref).max()))
