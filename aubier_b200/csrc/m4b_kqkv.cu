@@ -16,9 +16,19 @@
 // read twice: the K pass (all 576 columns, for MMA1) is released as soon as MMA1 consumed it,
 // and the V pass (the first 512 columns again, for MMA2) is re-read after the softmax -- from L2,
 // where the K pass left it (cache hint evict_last, re-read with evict_first).  HBM still sees
-// every KV byte once.  One FIFO ring of
-// five 32 KB slots carries, in consumption order, K(i+1) and V(i), so MMA1 of tile i+1 runs
-// while the softmax of tile i works (S and P are double-buffered).
+// every KV byte once.  Two rings of 32 KB slots carry the passes: the K ring (3 slots) the K
+// passes in tile order, the V ring (2 slots) the V passes, so MMA1 of tile i+1 runs while the
+// softmax of tile i works (S and P are double-buffered).
+//
+// Two MMA-issuing threads.  A tcgen05.mma of M = 128, N = 32 is short (~50 cycles of operand
+// reads), and the tensor pipe queues only a few of them: every barrier test, fence and commit of
+// a single issuing thread left the pipe idle, which paced the kernel at ~120 cycles per MMA.  So
+// MMA1 (S = K . Q) and MMA2 (O += V . P) are issued by two threads, each consuming its own ring
+// in order; while one waits or commits, the other's MMAs keep the pipe busy.  Each ring has one
+// producer and one consumer, so a slot's barrier is never more than one phase behind its waiter.
+// The orderings that one issuing thread used to give by program order are explicit barriers:
+// MMA1(t) waits until the softmax of tile t - 2 has read S[t & 1] (p_full), the softmax waits
+// for MMA2(t - 2) (o_done[t & 1]) before it rewrites P[t & 1].
 //
 // CTA = one split (a contiguous run of tiles, balanced as in m4-kqkv.cu:204-218), persistent,
 // one per SM.  Ragged batches (several tokens, each attending to its own window [base, base+len)
@@ -26,14 +36,16 @@
 // the tiles of all windows are concatenated and cut into balanced CTA ranges, so a CTA works
 // through a short list of segments (one per window it touches), restaging Q and writing one
 // partial record at every segment boundary.  The single-token op is the one-segment case.
-// Warp roles (320 threads):
-//   warp 0      TMA producer (ring loads)
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer; descriptors are precomputed,
+// Warp roles (384 threads):
+//   warp 0      TMA producer of the K ring (from HBM)
+//   warp 1      TMEM allocator + the MMA1 issuer (one thread); descriptors are precomputed,
 //               each MMA costs one 32-bit add to issue
 //   warps 2..9  softmax: two groups of four warps, group g owns heads 16g..16g+15; warp w reads
 //               TMEM lanes 32*(w%4).. (one key per thread), does the online softmax in log2 units
-//               with a lazy rescale of O (only when a head's max grows by more than 2^8), writes
+//               with a lazy rescale of O (only when a head's max grows by more than 2^15), writes
 //               P (f16) for MMA2, and writes the split's (o, m, l) partial record at the end.
+//   warp 10     the MMA2 issuer (one thread)
+//   warp 11     TMA producer of the V ring (from L2, once the tile's K pass has landed)
 // Numerics: q and P are rounded to f16 for the tensor cores -- the same rounding points as the
 // reference CPU graph, whose mul_mat converts an F32 src1 to F16 (ggml-cpu.c:1330-1375) -- and
 // both products accumulate in f32.
@@ -53,22 +65,13 @@ constexpr int H = kHeads;
 constexpr int TK = kTileKeys;           // 128 keys per tile
 constexpr int CHUNK_BYTES = TK * 128;   // 128 keys x 64 f16 columns = 16 KB, one SW128 TMA box
 constexpr int SLOT_BYTES = 2 * CHUNK_BYTES;
-constexpr int NSLOT = 5;                // FIFO ring: 5 x 32 KB
-// 1: each period's ring order puts half of tile i's V pass between tile i + 1's latent pairs and
-// its rope chunk, so the HBM reads of the K pass are spread over the period (Geo::K_SPLIT).
-// Measured on one box: 71.7-71.9 us at 262,144 keys against 67.3-68.0 us in the plain order (and
-// 140 against 124-126 us for the config-5 batch), so it is off.
-#ifndef M4B_KQ_INTERLEAVE
-#define M4B_KQ_INTERLEAVE 0
+#ifndef M4B_KQ_KSLOTS
+#define M4B_KQ_KSLOTS 3
 #endif
-// 1: every K pass and every V pass completes one barrier (each entry adds its bytes, the pass's
-// last entry arrives), so the MMA issuer tests one barrier per pass instead of one per entry;
-// slots are still released one entry at a time.  Measured on one box at 262,144 keys: 77.3-78.4 us
-// against 67.3-70.5 us with the per-entry waits (the issuer can no longer start a pass before all of
-// it has landed), so it is off.
-#ifndef M4B_KQ_PASS_WAIT
-#define M4B_KQ_PASS_WAIT 0
-#endif
+constexpr int NKSLOT = M4B_KQ_KSLOTS;   // K ring: 32 KB slots, filled from HBM
+constexpr int NVSLOT = 5 - NKSLOT;      // V ring: 32 KB slots, refilled from L2
+constexpr int NSLOT = NKSLOT + NVSLOT;  // K slots first, then V slots
+static_assert(NKSLOT >= 2 && NVSLOT >= 1, "both rings need slots");
 constexpr int QCH_BYTES = H * 128;      // 32 heads x 64 columns f16 = 4 KB
 constexpr int P_BYTES = 2 * QCH_BYTES;  // 32 heads x 128 keys f16 = 8 KB (double-buffered)
 constexpr int CTRL_BYTES = 2048;
@@ -85,10 +88,6 @@ struct Geo {
     static constexpr int LAT_PAIRS = R / 128;           // 4 or 2
     static constexpr int K_ENTRIES = LAT_PAIRS + 1;     // chunk pairs, then the rope chunk
     static constexpr int V_ENTRIES = LAT_PAIRS;
-    // Ring order of one period (tile i's V pass, tile i + 1's K pass): K entries [0, K_SPLIT),
-    // V entries [0, V_SPLIT), K entries [K_SPLIT, K_ENTRIES), V entries [V_SPLIT, V_ENTRIES).
-    static constexpr int K_SPLIT = M4B_KQ_INTERLEAVE ? LAT_PAIRS : K_ENTRIES;
-    static constexpr int V_SPLIT = M4B_KQ_INTERLEAVE ? V_ENTRIES / 2 : 0;
     static constexpr int PART = R + 4;                  // record: o[R], m, l, 2 pad
     static constexpr int PM = R;
     static constexpr int PL = R + 1;
@@ -113,7 +112,8 @@ struct Geo {
 using GeoBase = Geo<kLatent>;   // 512
 using GeoMistral = Geo<256>;
 
-constexpr int NTHREADS = 320;
+constexpr int NTHREADS = 384;
+constexpr int WARP_KLOAD = 0, WARP_MMA1 = 1, WARP_MMA2 = 10, WARP_VLOAD = 11;
 constexpr int TM_S = 0;
 constexpr int TM_O = 64;
 // log2 units: P = 2^(s - m) stays <= 2^15 (exact in f16, below its 65504 limit) while the running
@@ -133,12 +133,16 @@ struct Seg {
 };
 static_assert(sizeof(Seg) == 32, "segment table entry");
 
+// Barriers indexed [t & 1] complete one phase per tile of that parity: tile t is phase t >> 1.
 struct Ctrl {
-    uint64_t full[NSLOT];
-    uint64_t empty[NSLOT];
-    uint64_t kpass[2], vpass[2];   // M4B_KQ_PASS_WAIT: tile t's K / V pass landed ([t & 1], phase t >> 1)
-    uint64_t s_full[2], p_full[2];
-    uint64_t q_full, o_done, o_full;
+    uint64_t kfull[NKSLOT], kempty[NKSLOT];   // K ring: landed / released by MMA1
+    uint64_t vfull[NVSLOT], vempty[NVSLOT];   // V ring: landed / released by MMA2
+    uint64_t s_full[2];     // MMA1(t) complete: S[t & 1] holds tile t's scores
+    uint64_t p_full[2];     // the softmax of tile t wrote P[t & 1] (and has read S[t & 1])
+    uint64_t o_done[2];     // MMA2(t) complete: O holds tile t, P[t & 1] may be rewritten
+    uint64_t q_full;        // one phase per segment: its token's Q is staged
+    uint64_t o_full;        // the MMA2 issuer's last commit
+    uint64_t a_fin;         // the MMA1 issuer's last commit
     uint64_t red_full[2];   // per head group, once per tile: the 4 warps' flags / maxima are in
     uint64_t red2_full[2];  // per head group, rare: the exact maxima after a raised flag
     uint64_t redl_full[2];  // per head group: the 4 warps' row sums are in red_l[]
@@ -146,6 +150,7 @@ struct Ctrl {
     int abort_flag;
     int nseg;     // segments of this CTA
     int ntot;     // tiles of this CTA (sum over its segments)
+    int k_landed; // tiles whose K pass has landed (MMA1 issuer -> V producer; only grows)
     alignas(16) float red[2][2][4][16];  // [tile parity][group][quadrant][head], read as float4
     alignas(16) float red_l[2][4][16];   // [group][quadrant][head]
     alignas(16) int flag[2][2][4];       // [tile parity][group][quadrant]: a score outgrew the max
@@ -286,26 +291,30 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
     const int ncta = gridDim.x;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < NSLOT; ++i) {
-            mbar_init(&C.full[i], 1);
-            mbar_init(&C.empty[i], 1);
+        for (int i = 0; i < NKSLOT; ++i) {
+            mbar_init(&C.kfull[i], 1);
+            mbar_init(&C.kempty[i], 1);
+        }
+        for (int i = 0; i < NVSLOT; ++i) {
+            mbar_init(&C.vfull[i], 1);
+            mbar_init(&C.vempty[i], 1);
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&C.kpass[b], 1);
-            mbar_init(&C.vpass[b], 1);
             mbar_init(&C.s_full[b], 1);
             mbar_init(&C.p_full[b], 8);
+            mbar_init(&C.o_done[b], 1);
             mbar_init(&C.red_full[b], 4);
             mbar_init(&C.red2_full[b], 4);
             mbar_init(&C.redl_full[b], 4);
         }
         mbar_init(&C.q_full, 256);
-        mbar_init(&C.o_done, 1);
         mbar_init(&C.o_full, 1);
+        mbar_init(&C.a_fin, 1);
         C.abort_flag = 0;
+        C.k_landed = 0;
         fence_mbar_init();
     }
-    if (warp == 0) {
+    if (warp == WARP_KLOAD) {
         if (lane == 0) tma_prefetch_desc(&tmap);
         // ---- this CTA's segments
         if (p.seq_base == nullptr) {   // one window: the whole cache, masked by p.mask
@@ -355,7 +364,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
             }
         }
     }
-    if (warp == 1) {
+    if (warp == WARP_MMA1) {
         tmem_alloc(&C.tmem_base, G::TMEM_COLS);
         tmem_relinquish();
     }
@@ -372,187 +381,135 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
         return segs[g];
     };
 
-    if (warp == 0) {
-        // ------------------------------------------------------------------ TMA producer
+    if (warp == WARP_KLOAD || warp == WARP_VLOAD) {
+        // ------------------------------------------------------------------ TMA producers
+        // warp 0 feeds the K ring with every tile's K pass from HBM (kept in L2 for the V pass);
+        // warp 11 feeds the V ring with tile t's V pass once MMA1 has seen its K pass land, so
+        // the re-read hits L2.  Each is the only producer of its ring and fills it in order.
         if (lane == 0 && NT > 0) {
+            const bool kring = warp == WARP_KLOAD;
             if (!(p.flags & M4B_FLAG_KV_STATIC)) pdl_wait();
-            const uint64_t pol_keep = l2_policy_evict_last();    // K pass: V is re-read soon
-            const uint64_t pol_done = l2_policy_evict_first();   // V pass: last use
-            int slot = 0, phase = 0, issued = 0;
-            int kstarted = 0, kpasses = 0;  // K passes with an entry issued / with all issued
-            int vstarted = 0, vpasses = 0;
+            const uint64_t pol = kring ? l2_policy_evict_last()     // K pass: V is re-read soon
+                                       : l2_policy_evict_first();   // V pass: last use
+            uint64_t* const full = kring ? C.kfull : C.vfull;
+            uint64_t* const empty = kring ? C.kempty : C.vempty;
+            const int nslot = kring ? NKSLOT : NVSLOT;
+            const int nent = kring ? G::K_ENTRIES : G::V_ENTRIES;
+            uint8_t* const ring = smem + G::OFF_RING + (kring ? 0 : NKSLOT * SLOT_BYTES);
+            int slot = 0, phase = 0, issued = 0, g = 0;
             bool ok = true;
-            // one ring entry: chunks c0 (and c0 + 1 when two) of the tile at cache row key0; with
-            // pass barriers, `pass` collects the pass's bytes and `last` ends its phase
-            auto entry = [&](int key0, int c0, int two, uint64_t pol, uint64_t* pass, bool last) {
-                ok = ok && mbar_wait(&C.empty[slot], phase ^ 1, abort_flag);
-                if (!ok) return;
-                const uint32_t bytes = two ? SLOT_BYTES : CHUNK_BYTES;
-                uint64_t* bar = &C.full[slot];
-                if (M4B_KQ_PASS_WAIT) {
-                    bar = pass;
-                    if (last) mbar_arrive_expect_tx(bar, bytes);
-                    else mbar_expect_tx(bar, bytes);
-                } else {
-                    mbar_arrive_expect_tx(bar, bytes);
-                }
-                uint8_t* dst = smem + G::OFF_RING + slot * SLOT_BYTES;
-                tma_load_2d(dst, &tmap, 64 * c0, key0, bar, pol);
-                if (two) tma_load_2d(dst + CHUNK_BYTES, &tmap, 64 * (c0 + 1), key0, bar, pol);
-                ++issued;
-                if (++slot == NSLOT) {
-                    slot = 0;
-                    phase ^= 1;
-                }
-            };
-            int gk = 0, gv = 0;
-            // ring order = consumption order: K(0), then per tile i: K(i+1), V(i)
-            for (int t = -1; t < NT && ok; ++t) {
-                int kkey = -1, vkey = -1;
-                if (t + 1 < NT) {
-                    const Seg& sg = seg_of(t + 1, gk);
-                    kkey = sg.row0 + (t + 1 - sg.first) * TK;
-                }
-                if (t >= 0) {
-                    const Seg& sg = seg_of(t, gv);
-                    vkey = sg.row0 + (t - sg.first) * TK;
-                }
-                auto kpart = [&](int e0, int e1) {
-                    if (kkey < 0) return;
-                    for (int e = e0; e < e1 && ok; ++e) {
-                        entry(kkey, 2 * e, e < G::LAT_PAIRS, pol_keep, &C.kpass[(t + 1) & 1],
-                              e == G::K_ENTRIES - 1);
-                        if (ok && e == 0) ++kstarted;
-                        if (ok && e == G::K_ENTRIES - 1) ++kpasses;
+            for (int t = 0; t < NT && ok; ++t) {
+                const Seg& sg = seg_of(t, g);
+                const int key0 = sg.row0 + (t - sg.first) * TK;
+                if (!kring) ok = count_wait(&C.k_landed, t + 1, abort_flag);
+                // entry e: chunks 2e and 2e + 1 (columns 128e ..), or the rope chunk alone
+                for (int e = 0; e < nent && ok; ++e) {
+                    ok = mbar_wait(&empty[slot], phase ^ 1, abort_flag);
+                    if (!ok) break;
+                    const bool two = e < G::LAT_PAIRS;
+                    mbar_arrive_expect_tx(&full[slot], two ? SLOT_BYTES : CHUNK_BYTES);
+                    uint8_t* dst = ring + slot * SLOT_BYTES;
+                    tma_load_2d(dst, &tmap, 128 * e, key0, &full[slot], pol);
+                    if (two) tma_load_2d(dst + CHUNK_BYTES, &tmap, 128 * e + 64, key0, &full[slot], pol);
+                    ++issued;
+                    if (++slot == nslot) {
+                        slot = 0;
+                        phase ^= 1;
                     }
-                };
-                auto vpart = [&](int e0, int e1) {
-                    if (vkey < 0) return;
-                    for (int e = e0; e < e1 && ok; ++e) {
-                        entry(vkey, 2 * e, 1, pol_done, &C.vpass[t & 1], e == G::V_ENTRIES - 1);
-                        if (ok && e == 0) ++vstarted;
-                        if (ok && e == G::V_ENTRIES - 1) ++vpasses;
-                    }
-                };
-                kpart(0, G::K_SPLIT);
-                vpart(0, G::V_SPLIT);
-                kpart(G::K_SPLIT, G::K_ENTRIES);
-                vpart(G::V_SPLIT, G::V_ENTRIES);
+                }
             }
             if (*abort_flag) {
-                // let this CTA's own copies land before its shared memory is released
-                if (M4B_KQ_PASS_WAIT) {
-                    // a pass cut short gets its missing arrive, so its phase ends once the bytes
-                    // already requested have landed; then the last two passes of each kind
-                    if (kstarted > kpasses) mbar_arrive(&C.kpass[kpasses & 1]);
-                    if (vstarted > vpasses) mbar_arrive(&C.vpass[vpasses & 1]);
-                    for (int x = kstarted > 2 ? kstarted - 2 : 0; x < kstarted; ++x)
-                        mbar_drain(&C.kpass[x & 1], (x >> 1) & 1);
-                    for (int x = vstarted > 2 ? vstarted - 2 : 0; x < vstarted; ++x)
-                        mbar_drain(&C.vpass[x & 1], (x >> 1) & 1);
-                } else {
-                    for (int sl = 0; sl < NSLOT; ++sl) {
-                        const int n = issued > sl ? (issued - sl + NSLOT - 1) / NSLOT : 0;
-                        if (n > 0) mbar_drain(&C.full[sl], (n - 1) & 1);
-                    }
+                // let this CTA's own copies land before its shared memory is released: the
+                // latest use of every slot
+                for (int sl = 0; sl < nslot; ++sl) {
+                    const int n = issued > sl ? (issued - sl + nslot - 1) / nslot : 0;
+                    if (n > 0) mbar_drain(&full[sl], (n - 1) & 1);
                 }
             }
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------------ MMA issuer
+    } else if (warp == WARP_MMA1 || warp == WARP_MMA2) {
+        // ------------------------------------------------------------------ MMA issuers
         if (lane == 0) {
-            constexpr uint32_t idesc_s = idesc_f16_f32(128, 32, false, false);
-            constexpr uint32_t idesc_o = idesc_f16_f32(128, 32, true, false);
             constexpr uint32_t hi = sdesc_sw128_hi(1024);   // SBO = 8 rows x 128 B
-            // low descriptor halves; offsets below are in 16-byte units
-            const uint32_t lo_ringK = sdesc_sw128_lo(smem_u32(smem + G::OFF_RING), 16);
-            const uint32_t lo_ringMN = sdesc_sw128_lo(smem_u32(smem + G::OFF_RING), CHUNK_BYTES);
-            const uint32_t lo_q = sdesc_sw128_lo(smem_u32(smem + G::OFF_Q), 16);
-            const uint32_t lo_p = sdesc_sw128_lo(smem_u32(smem + G::OFF_P), 16);
             constexpr uint32_t U_CHUNK = CHUNK_BYTES >> 4, U_SLOT = SLOT_BYTES >> 4;
             constexpr uint32_t U_QCH = QCH_BYTES >> 4, U_P = P_BYTES >> 4;
-            int slot = 0, phase = 0;
+            int slot = 0, phase = 0, g = 0;
             bool ok = true;
-            auto take = [&]() -> uint32_t {   // wait for the next ring entry, return its slot
-                const uint32_t s_ = slot;
-                if (!M4B_KQ_PASS_WAIT) ok = ok && mbar_wait(&C.full[slot], phase, abort_flag);
-                if (++slot == NSLOT) {
-                    slot = 0;
-                    phase ^= 1;
-                }
-                return s_;
-            };
-            int g1 = 0, g2 = 0;
-            // MMA1 of tile t into S[t & 1]; the first tile of segment g waits for its Q
-            // K entries [e0, e1) of tile t (MMA1 into S[t & 1]): the first waits for the Q of
-            // a segment's first tile, the last signals S
-            auto mma1 = [&](int t, int e0, int e1) {
-                if (e0 >= e1) return;
-                const Seg& sg = seg_of(t, g1);
-                if (e0 == 0 && t == sg.first) ok = ok && mbar_wait(&C.q_full, g1 & 1, abort_flag);
-                if (M4B_KQ_PASS_WAIT && e0 == 0) {   // the whole K pass of tile t has landed
-                    ok = ok && mbar_wait(&C.kpass[t & 1], (t >> 1) & 1, abort_flag);
-                    if (!ok) return;
-                    tc_fence_after();
-                }
-                const uint32_t dS = tmem + TM_S + 32 * (t & 1);
-                for (int e = e0; e < e1 && ok; ++e) {
-                    const uint32_t sl = take();
-                    if (!ok) break;
-                    if (!M4B_KQ_PASS_WAIT) tc_fence_after();
-                    const uint32_t a = lo_ringK + sl * U_SLOT;
-                    const uint32_t b = lo_q + 2 * e * U_QCH;
+            if (warp == WARP_MMA1) {
+                // MMA1 of tile t into S[t & 1]: S^T[keys x heads] = K . Q^T, both K-major
+                constexpr uint32_t idesc_s = idesc_f16_f32(128, 32, false, false);
+                const uint32_t lo_ring = sdesc_sw128_lo(smem_u32(smem + G::OFF_RING), 16);
+                const uint32_t lo_q = sdesc_sw128_lo(smem_u32(smem + G::OFF_Q), 16);
+                for (int t = 0; t < NT && ok; ++t) {
+                    const Seg& sg = seg_of(t, g);
+                    // a segment's first tile needs its token's Q (segment g is q_full's phase g)
+                    if (t == sg.first) ok = mbar_wait(&C.q_full, g & 1, abort_flag);
+                    // S[t & 1] is free once the softmax of tile t - 2 has read it: it wrote P(t - 2)
+                    if (ok && t >= 2) ok = mbar_wait(&C.p_full[t & 1], ((t - 2) >> 1) & 1, abort_flag);
+                    const uint32_t dS = tmem + TM_S + 32 * (t & 1);
+                    for (int e = 0; e < G::K_ENTRIES && ok; ++e) {
+                        ok = mbar_wait(&C.kfull[slot], phase, abort_flag);
+                        if (!ok) break;
+                        tc_fence_after();
+                        const uint32_t a = lo_ring + slot * U_SLOT;
+                        const uint32_t b = lo_q + 2 * e * U_QCH;
 #pragma unroll
-                    for (int hf = 0; hf < 2; ++hf) {
-                        if (hf == 1 && e == G::LAT_PAIRS) break;
+                        for (int hf = 0; hf < 2; ++hf) {
+                            if (hf == 1 && e == G::LAT_PAIRS) break;
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            mma_f16(dS, sdesc_join(a + hf * U_CHUNK + 2 * kk, hi),
-                                    sdesc_join(b + hf * U_QCH + 2 * kk, hi), idesc_s,
-                                    (e | hf | kk) != 0 ? 1u : 0u);
+                            for (int kk = 0; kk < 4; ++kk)
+                                mma_f16(dS, sdesc_join(a + hf * U_CHUNK + 2 * kk, hi),
+                                        sdesc_join(b + hf * U_QCH + 2 * kk, hi), idesc_s,
+                                        (e | hf | kk) != 0 ? 1u : 0u);
+                        }
+                        mma_commit(&C.kempty[slot]);
+                        if (++slot == NKSLOT) {
+                            slot = 0;
+                            phase ^= 1;
+                        }
                     }
-                    mma_commit(&C.empty[sl]);
-                }
-                if (ok && e1 == G::K_ENTRIES) mma_commit(&C.s_full[t & 1]);
-            };
-            // V entries [b0, b1) of tile i (MMA2 into those latent blocks): the first needs P(i);
-            // the first tile of a segment starts a fresh accumulator; the last signals o_done
-            auto mma2 = [&](int i, int b0, int b1) {
-                if (b0 >= b1 || !ok) return;
-                const Seg& sg = seg_of(i, g2);
-                if (b0 == 0) {
-                    ok = mbar_wait(&C.p_full[i & 1], (i >> 1) & 1, abort_flag);
-                    if (M4B_KQ_PASS_WAIT)   // the whole V pass of tile i has landed
-                        ok = ok && mbar_wait(&C.vpass[i & 1], (i >> 1) & 1, abort_flag);
-                    if (!ok) return;
-                    tc_fence_after();
-                }
-                const uint32_t p0 = lo_p + (i & 1) * U_P;
-                const uint32_t acc0 = i != sg.first ? 1u : 0u;
-                for (int b = b0; b < b1 && ok; ++b) {
-                    const uint32_t sl = take();
                     if (!ok) break;
-                    if (!M4B_KQ_PASS_WAIT) tc_fence_after();
-                    const uint32_t a0 = lo_ringMN + sl * U_SLOT;
-#pragma unroll
-                    for (int ks = 0; ks < 8; ++ks)
-                        mma_f16(tmem + TM_O + 32 * b, sdesc_join(a0 + ks * (2048 >> 4), hi),
-                                sdesc_join(p0 + (ks >> 2) * U_QCH + 2 * (ks & 3), hi), idesc_o,
-                                ks > 0 ? 1u : acc0);
-                    mma_commit(&C.empty[sl]);
+                    mma_commit(&C.s_full[t & 1]);
+                    *reinterpret_cast<volatile int*>(&C.k_landed) = t + 1;   // its V pass may go
                 }
-                if (ok && b1 == G::V_ENTRIES) mma_commit(&C.o_done);
-            };
-            if (NT > 0) mma1(0, 0, G::K_ENTRIES);
-            for (int i = 0; i < NT && ok; ++i) {
-                // period i in ring order: MMA1 of tile i + 1 and MMA2 of tile i
-                const bool more = i + 1 < NT;
-                if (more) mma1(i + 1, 0, G::K_SPLIT);
-                mma2(i, 0, G::V_SPLIT);
-                if (more) mma1(i + 1, G::K_SPLIT, G::K_ENTRIES);
-                mma2(i, G::V_SPLIT, G::V_ENTRIES);
+                // every MMA1 of this thread has completed before the CTA frees TMEM
+                mma_commit(&C.a_fin);
+                mbar_drain(&C.a_fin, 0);
+            } else {
+                // MMA2 of tile i: O^T[latent block x heads] += V^T . P, V read MN-major from the
+                // V pass itself; the first tile of a segment starts a fresh accumulator
+                constexpr uint32_t idesc_o = idesc_f16_f32(128, 32, true, false);
+                const uint32_t lo_ring = sdesc_sw128_lo(smem_u32(smem + G::OFF_RING + NKSLOT * SLOT_BYTES),
+                                                        CHUNK_BYTES);
+                const uint32_t lo_p = sdesc_sw128_lo(smem_u32(smem + G::OFF_P), 16);
+                for (int i = 0; i < NT && ok; ++i) {
+                    const Seg& sg = seg_of(i, g);
+                    ok = mbar_wait(&C.p_full[i & 1], (i >> 1) & 1, abort_flag);
+                    if (!ok) break;
+                    const uint32_t p0 = lo_p + (i & 1) * U_P;
+                    const uint32_t acc0 = i != sg.first ? 1u : 0u;
+                    for (int b = 0; b < G::V_ENTRIES && ok; ++b) {
+                        ok = mbar_wait(&C.vfull[slot], phase, abort_flag);
+                        if (!ok) break;
+                        tc_fence_after();
+                        const uint32_t a0 = lo_ring + slot * U_SLOT;
+#pragma unroll
+                        for (int ks = 0; ks < 8; ++ks)
+                            mma_f16(tmem + TM_O + 32 * b, sdesc_join(a0 + ks * (2048 >> 4), hi),
+                                    sdesc_join(p0 + (ks >> 2) * U_QCH + 2 * (ks & 3), hi), idesc_o,
+                                    ks > 0 ? 1u : acc0);
+                        mma_commit(&C.vempty[slot]);
+                        if (++slot == NVSLOT) {
+                            slot = 0;
+                            phase ^= 1;
+                        }
+                    }
+                    if (!ok) break;
+                    mma_commit(&C.o_done[i & 1]);
+                }
+                mma_commit(&C.o_full);
+                mbar_drain(&C.o_full, 0);
             }
-            mma_commit(&C.o_full);
         }
     } else {
         // ------------------------------------------------------------------ softmax warps
@@ -567,7 +524,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
         // one L2 round trip instead of nine dependent ones, which matters because the ring has HBM
         // saturated by then (nine round trips measured ~6.6 us, stalling the first MMA).  At a
         // window boundary inside the tile loop, where the softmax state is live, the loads go in
-        // two batches (5 + 4 units at BASELINE) to stay within the 168 registers that 10 warps per SM allow
+        // two batches (5 + 4 units at BASELINE) to stay within the 168 registers that 12 warps per SM allow
         // (3 warps share one 16K-register sub-partition).
         auto stage_q = [&](const float* qs, bool one_batch) {
             constexpr int D = G::D;
@@ -754,9 +711,17 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
                     }
                 }
             }
+            // P[i & 1] is free once MMA2(i - 2) has completed.  o_done[i & 1] is then at most
+            // one phase behind (the wait of tile i - 2 saw tile i - 4's phase) and cannot be
+            // ahead (tile i's phase needs this P), so the parity wait is exact; the same holds
+            // for the waits on o_done below.
+            if (i >= 2) {
+                ok = warp_wait(&C.o_done[i & 1], ((i - 2) >> 1) & 1, abort_flag);
+                if (!ok) break;
+            }
             if (need) {   // uniform across the group: every thread computed the same maxima
                 // O holds the sum through tile i-1 (same segment): wait for MMA2(i-1)
-                ok = warp_wait(&C.o_done, (i - 1) & 1, abort_flag);
+                ok = warp_wait(&C.o_done[(i - 1) & 1], ((i - 1) >> 1) & 1, abort_flag);
                 if (!ok) break;
                 tc_fence_after();
 #pragma unroll
@@ -790,14 +755,9 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
             if (lane == 0) mbar_arrive(&C.p_full[i & 1]);
             if (seg_end && g + 1 < nseg) {
                 // a segment other than the last ends here: write its record once MMA2(i) is
-                // done (the next segment's MMA2 waits for P(i+1), written after this).  o_done
-                // completes one phase per MMA2, and a parity wait cannot tell phase i from phase
-                // i - 2.  Here phases up to i - 2 are complete (MMA2(i-2) was issued before
-                // MMA1(i), whose S this thread has read), but MMA2(i-1) may still run: wait for
-                // phase i - 1 first, so that the wait for phase i is not answered by phase i - 2.
-                ok = warp_wait(&C.o_done, (i - 1) & 1, abort_flag);
-                if (!ok) break;
-                flush(sg, &C.o_done, i & 1);
+                // done (the next segment's MMA2 waits for P(i+1), written after this).  MMA2(i)
+                // completing means the MMA2 thread's earlier MMAs have completed too.
+                flush(sg, &C.o_done[i & 1], (i >> 1) & 1);
                 if (!ok) break;
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
@@ -812,7 +772,7 @@ kqkv_partial_kernel(const __grid_constant__ CUtensorMap tmap, const KqParams p) 
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == WARP_MMA1) {
         tc_fence_after();
         tmem_dealloc(tmem, G::TMEM_COLS);
     }

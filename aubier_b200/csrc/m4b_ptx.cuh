@@ -113,8 +113,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
-// Wait used only on the abort path to let this CTA's own in-flight TMA copies land before it
-// exits (bounded; ignores the abort flag).
+// Bounded wait until a shared-memory counter that only grows reaches `target` (one thread polls;
+// a counter, unlike a barrier's phase parity, cannot be mistaken for an older value).
+__device__ __forceinline__ bool count_wait(const int* counter, int target, volatile int* abort_flag) {
+    const volatile int* c = counter;
+    if (*c >= target) return true;
+    const long long t0 = clock64();
+    while (true) {
+        __nanosleep(32);
+        if (*c >= target) return true;
+        if (*abort_flag) return false;
+        if (wait_expired(t0)) {
+            *abort_flag = 1;
+            atomicExch(&g_status, DEV_STATUS_TIMEOUT);
+            return false;
+        }
+    }
+}
+
+// Wait used on the abort path to let this CTA's own in-flight TMA copies land before it exits,
+// and by each MMA issuer for its own last commit (bounded; ignores the abort flag).
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
     const uint32_t addr = smem_u32(bar);
     const long long t0 = clock64();
