@@ -11,7 +11,7 @@ into one record per head and stores it into every peer over NVLink (fused exchan
 nccl uses an NCCL all-gather instead), then merges all ranks' records and applies W_UV.
 
 --config 2 / 3: the same step at 4,096 / 32,768 keys (at N=1 the default run also measures both
-and reports them under "other_configs").
+and reports them under "other_configs"; at every N it also measures config 5 there).
 --config 5: ragged batched decode, 16 sequences with one new token each, lengths uniform on
 [512, 65536] by seed, one packed cache per layer with per-sequence base/length; whole sequences
 per rank (LPT on keys), no exchange.  A layer-step covers all 16 sequences.
@@ -711,20 +711,24 @@ def run_ours(args, rank: int, world: int) -> None:
     del w
     torch.cuda.empty_cache()
 
-    # configs 2 and 3 (4,096 and 32,768 keys, 36 layers) beside the headline, on one GPU
+    # beside the headline: configs 2 and 3 (4,096 and 32,768 keys, 36 layers) on one GPU, and
+    # config 5 (16 ragged sequences, sharded by sequence over the ranks) at every GPU count
     others = []
-    if (world == 1 and args.config == 4 and args.geometry == "baseline" and args.keys == 262144
+    if (args.config == 4 and args.geometry == "baseline" and args.keys == 262144
             and not args.no_other_configs):
-        for cfg in (2, 3):
+        for cfg in ((2, 3, 5) if world == 1 else (5,)):
             a2 = copy.copy(args)
-            a2.keys = CONFIG_KEYS[cfg]
-            w2 = slab_workload(a2, rank, world, dev)
+            a2.config = cfg
+            a2.keys = CONFIG_KEYS.get(cfg, args.keys)
+            w2 = (ragged_workload if cfg == 5 else slab_workload)(a2, rank, world, dev)
             r2 = measure(w2, a2, rank, world, dev, sample_clocks=False)
+            w2.close()
             r2 = {"config": cfg, "metric": w2.metric, "value": r2["value"], "unit": UNIT,
                   "ms_per_step": r2["ms_per_step"], "e2e": r2["e2e"], "roofline": r2["roofline"],
                   "hbm_gbs_step": r2["hbm_gbs_step"], "parity": r2["parity"],
-                  "workload": w2.config["workload"]}
-            if not args.no_cpu_baseline:
+                  "workload": w2.config["workload"], "parallelism": w2.config.get("parallelism"),
+                  "gpu_launches": w2.launches_per_step * a2.steps}
+            if world == 1 and not args.no_cpu_baseline:
                 r2["cpu_baseline"] = cpu_baseline_of(w2.lengths, 20)
             others.append(r2)
             del w2
@@ -785,7 +789,8 @@ def main():
     ap.add_argument("--cpu-reps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-other-configs", action="store_true",
-                    help="config 4 at N=1: skip the configs 2 and 3 lines beside the headline")
+                    help="config 4: skip the lines beside the headline (configs 2 and 3 at N=1, "
+                         "config 5 at every N)")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="config 4, N>1: fused NVLink exchange in the merge kernels, or NCCL")
     ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=4,
