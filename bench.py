@@ -720,9 +720,14 @@ def run_ours(args, rank: int, world: int) -> None:
             a2 = copy.copy(args)
             a2.config = cfg
             a2.keys = CONFIG_KEYS.get(cfg, args.keys)
-            w2 = (ragged_workload if cfg == 5 else slab_workload)(a2, rank, world, dev)
-            r2 = measure(w2, a2, rank, world, dev, sample_clocks=False)
-            w2.close()
+            try:   # a failure that every rank meets alike costs this entry, not the headline line
+                w2 = (ragged_workload if cfg == 5 else slab_workload)(a2, rank, world, dev)
+                r2 = measure(w2, a2, rank, world, dev, sample_clocks=False)
+                w2.close()
+            except Exception as e:     # noqa: BLE001 -- reported in the JSON line
+                others.append({"config": cfg, "error": f"{type(e).__name__}: {e}"[:300]})
+                torch.cuda.empty_cache()
+                continue
             r2 = {"config": cfg, "metric": w2.metric, "value": r2["value"], "unit": UNIT,
                   "ms_per_step": r2["ms_per_step"], "e2e": r2["e2e"], "roofline": r2["roofline"],
                   "hbm_gbs_step": r2["hbm_gbs_step"], "parity": r2["parity"],
