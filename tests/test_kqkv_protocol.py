@@ -1,0 +1,312 @@
+"""CPU model of kqkv_partial_kernel's synchronisation protocol (aubier_b200/csrc/m4b_kqkv.cu), run
+under random schedules.
+
+The kernel's roles -- K producer, V producer, MMA1 issuer, MMA2 issuer, softmax -- are modelled as
+sequential programs over mbarriers with the hardware's parity semantics: a barrier counts completed
+phases, and a wait for phase k with parity k & 1 succeeds once the count's parity differs from
+k & 1.  Such a wait is only sound if, when it starts, the barrier has completed k or k + 1 phases:
+with k - 1 it would succeed at once on an older phase, with k + 2 it would wait for a later one.
+TMA loads land, and each issuing thread's MMAs and commits complete, asynchronously (an issuing
+thread's operations complete in issue order).  The scheduler interleaves everything at random.
+
+Checked in every schedule:
+  * every parity wait starts with its barrier k or k + 1 phases complete, and ends on phase k;
+  * no ring slot is refilled while an MMA still reads it, no P buffer is rewritten while MMA2 reads
+    it, no S buffer is overwritten before the softmax has read it, O is not rescaled or restarted
+    while an MMA2 into it is in flight, and a segment's record is read only after its last MMA2;
+  * the program finishes (no deadlock).
+
+Two planted mistakes must be caught (they live in the model, on the CPU): the one-issuer build's
+single o_done barrier (one phase per tile) with the flush's direct wait, and the softmax rewriting
+P without waiting for MMA2 two tiles back -- an ordering that one issuing thread gave for free.
+"""
+import random
+
+import pytest
+
+
+class ProtocolError(AssertionError):
+    pass
+
+
+class Barrier:
+    def __init__(self, name, count=1):
+        self.name, self.count, self.pending, self.done = name, count, count, 0
+
+    def arrive(self):
+        self.pending -= 1
+        if self.pending == 0:
+            self.done += 1
+            self.pending = self.count
+
+
+class Wait:
+    """A role's request to wait for phase `k` of `bar` (parity k & 1)."""
+
+    def __init__(self, bar, k):
+        self.bar, self.k, self.checked = bar, k, False
+
+    def ready(self):
+        if not self.checked:
+            self.checked = True
+            if self.bar.done not in (self.k, self.k + 1):
+                raise ProtocolError(f"wait for phase {self.k} of {self.bar.name} starts with "
+                                    f"{self.bar.done} phases complete")
+        ok = (self.bar.done & 1) != (self.k & 1)
+        if ok and self.bar.done != self.k + 1:
+            raise ProtocolError(f"wait for phase {self.k} of {self.bar.name} ended on phase "
+                                f"{self.bar.done - 1}")
+        return ok
+
+
+class CountWait:
+    def __init__(self, get, target):
+        self.get, self.target = get, target
+
+    def ready(self):
+        return self.get() >= self.target
+
+
+class Model:
+    def __init__(self, segs, k_entries, v_entries, nk, nv, rng, single_o_done=False,
+                 rescale_p=0.3, p_free_wait=True):
+        self.rng = rng
+        self.segs = segs                      # tiles per segment
+        self.NT = sum(segs)
+        self.first = []                       # tile -> its segment's first tile
+        self.seg_of = []
+        for g, n in enumerate(segs):
+            start = sum(segs[:g])
+            for _ in range(n):
+                self.first.append(start)
+                self.seg_of.append(g)
+        self.KE, self.VE, self.NK, self.NV = k_entries, v_entries, nk, nv
+        self.single = single_o_done
+        self.rescale_p = rescale_p
+        self.p_free_wait = p_free_wait
+        B = Barrier
+        self.kfull = [B(f"kfull{i}") for i in range(nk)]
+        self.kempty = [B(f"kempty{i}") for i in range(nk)]
+        self.vfull = [B(f"vfull{i}") for i in range(nv)]
+        self.vempty = [B(f"vempty{i}") for i in range(nv)]
+        self.s_full = [B("s_full0"), B("s_full1")]
+        self.p_full = [B("p_full0"), B("p_full1")]
+        self.o_done = [B("o_done")] if single_o_done else [B("o_done0"), B("o_done1")]
+        self.q_full, self.o_full, self.a_fin = B("q_full"), B("o_full"), B("a_fin")
+        self.k_landed = 0
+        # state for the hazard checks
+        self.slot_readers = {}                # ("K"/"V", slot) -> MMAs in flight reading it
+        self.p_readers = [0, 0]               # MMA2s in flight reading P[b]
+        self.o_writers = 0                    # MMA2s in flight into O
+        self.s_writers = [0, 0]               # MMA1s in flight into S[b]
+        self.s_read = [-1, -1]                # last tile whose S[b] the softmax has read
+        self.tma = []                         # (barrier, key) loads in flight
+        self.queues = {"A": [], "B": []}      # each issuer's operations in issue order
+        self.roles = {n: f() for n, f in (("kload", self.kload), ("vload", self.vload),
+                                          ("mma1", self.mma1), ("mma2", self.mma2),
+                                          ("softmax", self.softmax))}
+        self.waiting = {}
+
+    # ---- parity helpers: wait for phase k of a barrier
+    def od(self, tile):                       # o_done barrier and phase for MMA2(tile)
+        if self.single:
+            return self.o_done[0], tile
+        return self.o_done[tile & 1], tile >> 1
+
+    # ---- roles (generators yielding waits)
+    def kload(self):
+        slot = use = 0
+        for t in range(self.NT):
+            for e in range(self.KE):
+                yield Wait(self.kempty[slot], use - 1) if use > 0 else None
+                if self.slot_readers.get(("K", slot), 0):
+                    raise ProtocolError(f"K slot {slot} refilled while an MMA reads it")
+                self.tma.append((self.kfull[slot], ("K", slot)))
+                slot += 1
+                if slot == self.NK:
+                    slot, use = 0, use + 1
+
+    def vload(self):
+        slot = use = 0
+        for t in range(self.NT):
+            yield CountWait(lambda: self.k_landed, t + 1)
+            for e in range(self.VE):
+                yield Wait(self.vempty[slot], use - 1) if use > 0 else None
+                if self.slot_readers.get(("V", slot), 0):
+                    raise ProtocolError(f"V slot {slot} refilled while an MMA reads it")
+                self.tma.append((self.vfull[slot], ("V", slot)))
+                slot += 1
+                if slot == self.NV:
+                    slot, use = 0, use + 1
+
+    def issue(self, q, kind, **kw):
+        self.queues[q].append((kind, kw))
+
+    def mma1(self):
+        slot = use = 0
+        for t in range(self.NT):
+            if t == self.first[t]:
+                yield Wait(self.q_full, self.seg_of[t])
+            if t >= 2:
+                yield Wait(self.p_full[t & 1], (t - 2) >> 1)
+            if self.s_read[t & 1] < t - 2:
+                raise ProtocolError(f"MMA1({t}) overwrites S before the softmax read tile {t - 2}")
+            for e in range(self.KE):
+                yield Wait(self.kfull[slot], use)
+                self.slot_readers[("K", slot)] = self.slot_readers.get(("K", slot), 0) + 1
+                self.s_writers[t & 1] += 1
+                self.issue("A", "mma1", slot=slot, b=t & 1)
+                self.issue("A", "commit", bar=self.kempty[slot])
+                slot += 1
+                if slot == self.NK:
+                    slot, use = 0, use + 1
+            self.issue("A", "commit", bar=self.s_full[t & 1])
+            self.k_landed = t + 1
+        self.issue("A", "commit", bar=self.a_fin)
+        yield Wait(self.a_fin, 0)
+
+    def mma2(self):
+        slot = use = 0
+        for i in range(self.NT):
+            yield Wait(self.p_full[i & 1], i >> 1)
+            for b in range(self.VE):
+                yield Wait(self.vfull[slot], use)
+                if b == 0 and i == self.first[i] and self.flushing:
+                    raise ProtocolError(f"MMA2({i}) restarts O while the record is read")
+                self.slot_readers[("V", slot)] = self.slot_readers.get(("V", slot), 0) + 1
+                self.p_readers[i & 1] += 1
+                self.o_writers += 1
+                self.issue("B", "mma2", slot=slot, b=i & 1)
+                self.issue("B", "commit", bar=self.vempty[slot])
+                slot += 1
+                if slot == self.NV:
+                    slot, use = 0, use + 1
+            bar, _ = self.od(i)
+            self.issue("B", "commit", bar=bar)
+        self.issue("B", "commit", bar=self.o_full)
+        yield Wait(self.o_full, 0)
+
+    flushing = False
+
+    def softmax(self):
+        nseg = len(self.segs)
+        if self.NT > 0:
+            self.q_full.arrive()              # the first segment's Q, staged before the loop
+        for i in range(self.NT):
+            g = self.seg_of[i]
+            yield Wait(self.s_full[i & 1], i >> 1)
+            if self.s_writers[i & 1]:
+                raise ProtocolError(f"softmax reads S({i}) with an MMA1 into it in flight")
+            self.s_read[i & 1] = i
+            seg_end = i == self.first[i] + self.segs[g] - 1
+            if seg_end and g + 1 < nseg:
+                self.q_full.arrive()          # the next segment's Q (MMA1(i) is complete)
+            if not self.single and self.p_free_wait and i >= 2:
+                bar, k = self.od(i - 2)
+                yield Wait(bar, k)            # P[i & 1] free: MMA2(i - 2) complete
+            if i > self.first[i] and self.rng.random() < self.rescale_p:
+                bar, k = self.od(i - 1)
+                yield Wait(bar, k)            # rescale O: MMA2(i - 1) complete
+                if self.o_writers:
+                    raise ProtocolError(f"O rescaled at tile {i} with an MMA2 in flight")
+            if self.p_readers[i & 1]:
+                raise ProtocolError(f"P({i}) written while MMA2 reads P[{i & 1}]")
+            self.p_full[i & 1].arrive()
+            if seg_end and g + 1 < nseg:
+                if self.single:               # the one-issuer build: a direct wait for phase i
+                    yield Wait(self.o_done[0], i)
+                else:
+                    bar, k = self.od(i)
+                    yield Wait(bar, k)
+                if self.o_writers:
+                    raise ProtocolError(f"record of tile {i} read with an MMA2 in flight")
+                self.flushing = True
+                yield None                    # reading O out of TMEM takes a while
+                self.flushing = False
+        if self.segs:
+            yield Wait(self.o_full, 0)
+            if self.o_writers:
+                raise ProtocolError("last record read with an MMA2 in flight")
+
+    # ---- async completions
+    def complete_tma(self, j):
+        bar, _ = self.tma.pop(j)
+        bar.arrive()
+
+    def complete_op(self, q):
+        kind, kw = self.queues[q].pop(0)
+        if kind == "mma1":
+            self.slot_readers[("K", kw["slot"])] -= 1
+            self.s_writers[kw["b"]] -= 1
+        elif kind == "mma2":
+            self.slot_readers[("V", kw["slot"])] -= 1
+            self.p_readers[kw["b"]] -= 1
+            self.o_writers -= 1
+        else:
+            kw["bar"].arrive()
+
+    def run(self, max_steps=200000):
+        live = dict(self.roles)
+        for _ in range(max_steps):
+            moves = []
+            for name, gen in live.items():
+                w = self.waiting.get(name)
+                if w is None or w.ready():
+                    moves.append(("role", name))
+            moves += [("tma", j) for j in range(len(self.tma))]
+            moves += [("op", q) for q in self.queues if self.queues[q]]
+            if not moves:
+                if live:
+                    raise ProtocolError(f"deadlock: {sorted(live)} wait")
+                return
+            kind, x = self.rng.choice(moves)
+            if kind == "tma":
+                self.complete_tma(x)
+            elif kind == "op":
+                self.complete_op(x)
+            else:
+                self.waiting.pop(x, None)
+                try:
+                    w = next(live[x])
+                    if w is not None:
+                        self.waiting[x] = w
+                except StopIteration:
+                    del live[x]
+        raise ProtocolError("no progress bound reached")
+
+
+SEGMENTS = [[1], [2], [3], [7], [1, 1], [1, 2, 1], [2, 1, 3], [1, 1, 1, 1], [5, 1], [0]]
+
+
+@pytest.mark.parametrize("geo", [(5, 4, 3, 2), (3, 2, 3, 2)], ids=["latent512", "latent256"])
+def test_two_issuer_protocol_holds_under_random_schedules(geo):
+    ke, ve, nk, nv = geo
+    rng = random.Random(20261202)
+    for segs in SEGMENTS:                     # [0]: a split with no tiles still writes its record
+        for _ in range(150):
+            Model(segs, ke, ve, nk, nv, rng).run()
+
+
+def test_planted_single_o_done_barrier_is_caught():
+    """The one-issuer build's single o_done barrier, waited with one parity per tile, is unsound
+    once MMA2 has its own issuing thread: some schedule must trip the checker."""
+    rng = random.Random(7)
+    caught = 0
+    for _ in range(400):
+        try:
+            Model([1, 2, 3], 5, 4, 3, 2, rng, single_o_done=True, rescale_p=0.5).run()
+        except ProtocolError:
+            caught += 1
+    assert caught > 0
+
+
+def test_planted_missing_p_free_wait_is_caught():
+    rng = random.Random(3)
+    caught = 0
+    for _ in range(1500):
+        try:
+            Model([2, 3], 5, 4, 3, 2, rng, p_free_wait=False).run()
+        except ProtocolError as e:
+            assert "P(" in str(e) or "phase" in str(e)
+            caught += 1
+    assert caught > 0
