@@ -69,7 +69,7 @@ class CountWait:
 
 class Model:
     def __init__(self, segs, k_entries, v_entries, nk, nv, rng, single_o_done=False,
-                 rescale_p=0.3, p_free_wait=True):
+                 rescale_p=0.3, p_free_wait=True, shared_ring=False):
         self.rng = rng
         self.segs = segs                      # tiles per segment
         self.NT = sum(segs)
@@ -84,6 +84,18 @@ class Model:
         self.single = single_o_done
         self.rescale_p = rescale_p
         self.p_free_wait = p_free_wait
+        # shared_ring: the earlier two-issuer variant -- one FIFO ring of nk + nv slots filled in
+        # consumption order K(0), then K(t + 1), V(t) per tile, taken by both issuers
+        self.shared = shared_ring
+        if shared_ring:
+            order = [("K", 0, e) for e in range(k_entries)] if self.NT else []
+            for t in range(self.NT):
+                if t + 1 < self.NT:
+                    order += [("K", t + 1, e) for e in range(k_entries)]
+                order += [("V", t, e) for e in range(v_entries)]
+            self.order = order
+            self.entry = {x: j for j, x in enumerate(order)}
+            self.RS = nk + nv
         B = Barrier
         self.kfull = [B(f"kfull{i}") for i in range(nk)]
         self.kempty = [B(f"kempty{i}") for i in range(nk)]
@@ -102,9 +114,13 @@ class Model:
         self.s_read = [-1, -1]                # last tile whose S[b] the softmax has read
         self.tma = []                         # (barrier, key) loads in flight
         self.queues = {"A": [], "B": []}      # each issuer's operations in issue order
-        self.roles = {n: f() for n, f in (("kload", self.kload), ("vload", self.vload),
-                                          ("mma1", self.mma1), ("mma2", self.mma2),
-                                          ("softmax", self.softmax))}
+        loaders = ((("load", self.load),) if shared_ring else
+                   (("kload", self.kload), ("vload", self.vload)))
+        if shared_ring:
+            self.full = [B(f"full{i}") for i in range(self.RS)]
+            self.empty = [B(f"empty{i}") for i in range(self.RS)]
+        self.roles = {n: f() for n, f in loaders + (("mma1", self.mma1), ("mma2", self.mma2),
+                                                    ("softmax", self.softmax))}
         self.waiting = {}
 
     # ---- parity helpers: wait for phase k of a barrier
@@ -139,6 +155,24 @@ class Model:
                 if slot == self.NV:
                     slot, use = 0, use + 1
 
+    def load(self):                           # shared_ring: one producer, one ring
+        for j in range(len(self.order)):
+            slot, use = j % self.RS, j // self.RS
+            yield Wait(self.empty[slot], use - 1) if use > 0 else None
+            if self.slot_readers.get(("R", slot), 0):
+                raise ProtocolError(f"ring slot {slot} refilled while an MMA reads it")
+            self.tma.append((self.full[slot], ("R", slot)))
+
+    def take(self, kind, t, e, slot, use):
+        """The slot an issuer consumes next: (barrier, phase, reader key, release barrier)."""
+        if self.shared:
+            j = self.entry[(kind, t, e)]
+            r = j % self.RS
+            return self.full[r], j // self.RS, ("R", r), self.empty[r]
+        if kind == "K":
+            return self.kfull[slot], use, ("K", slot), self.kempty[slot]
+        return self.vfull[slot], use, ("V", slot), self.vempty[slot]
+
     def issue(self, q, kind, **kw):
         self.queues[q].append((kind, kw))
 
@@ -152,11 +186,12 @@ class Model:
             if self.s_read[t & 1] < t - 2:
                 raise ProtocolError(f"MMA1({t}) overwrites S before the softmax read tile {t - 2}")
             for e in range(self.KE):
-                yield Wait(self.kfull[slot], use)
-                self.slot_readers[("K", slot)] = self.slot_readers.get(("K", slot), 0) + 1
+                full, ph, key, empty = self.take("K", t, e, slot, use)
+                yield Wait(full, ph)
+                self.slot_readers[key] = self.slot_readers.get(key, 0) + 1
                 self.s_writers[t & 1] += 1
-                self.issue("A", "mma1", slot=slot, b=t & 1)
-                self.issue("A", "commit", bar=self.kempty[slot])
+                self.issue("A", "mma1", key=key, b=t & 1)
+                self.issue("A", "commit", bar=empty)
                 slot += 1
                 if slot == self.NK:
                     slot, use = 0, use + 1
@@ -170,14 +205,15 @@ class Model:
         for i in range(self.NT):
             yield Wait(self.p_full[i & 1], i >> 1)
             for b in range(self.VE):
-                yield Wait(self.vfull[slot], use)
+                full, ph, key, empty = self.take("V", i, b, slot, use)
+                yield Wait(full, ph)
                 if b == 0 and i == self.first[i] and self.flushing:
                     raise ProtocolError(f"MMA2({i}) restarts O while the record is read")
-                self.slot_readers[("V", slot)] = self.slot_readers.get(("V", slot), 0) + 1
+                self.slot_readers[key] = self.slot_readers.get(key, 0) + 1
                 self.p_readers[i & 1] += 1
                 self.o_writers += 1
-                self.issue("B", "mma2", slot=slot, b=i & 1)
-                self.issue("B", "commit", bar=self.vempty[slot])
+                self.issue("B", "mma2", key=key, b=i & 1)
+                self.issue("B", "commit", bar=empty)
                 slot += 1
                 if slot == self.NV:
                     slot, use = 0, use + 1
@@ -236,10 +272,10 @@ class Model:
     def complete_op(self, q):
         kind, kw = self.queues[q].pop(0)
         if kind == "mma1":
-            self.slot_readers[("K", kw["slot"])] -= 1
+            self.slot_readers[kw["key"]] -= 1
             self.s_writers[kw["b"]] -= 1
         elif kind == "mma2":
-            self.slot_readers[("V", kw["slot"])] -= 1
+            self.slot_readers[kw["key"]] -= 1
             self.p_readers[kw["b"]] -= 1
             self.o_writers -= 1
         else:
@@ -310,3 +346,18 @@ def test_planted_missing_p_free_wait_is_caught():
             assert "P(" in str(e) or "phase" in str(e)
             caught += 1
     assert caught > 0
+
+
+def test_shared_ring_of_the_earlier_two_issuer_variant_aliases():
+    """The earlier two-issuer variant (not in the library; it failed at full size) let both issuers
+    take entries from one FIFO ring.  An issuer running ahead of the other then waits on a slot whose
+    previous use, the other issuer's, has not landed: some schedule must show the stale parity."""
+    rng = random.Random(11)
+    caught = []
+    for _ in range(600):
+        try:
+            Model([14], 5, 4, 3, 2, rng, shared_ring=True).run()
+        except ProtocolError as e:
+            caught.append(str(e))
+    assert caught, "the shared ring never aliased"
+    assert any("full" in c for c in caught)
