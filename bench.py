@@ -275,8 +275,9 @@ def slab_workload(args, rank, world, dev):
         torch.cuda.synchronize()            # every rank's inputs exist before the first exchange
         dist.barrier()
     flags = m4.FLAG_PDL
-    # short slabs: the merge releases the next layer's launch once its W_UV loads are issued
-    early = m4.FLAG_EARLY_RELEASE if n_loc <= 131072 else 0
+    # the merge releases the next layer's launch once its W_UV loads are issued (with the
+    # two-issuer KQKV this gains at every slab size, 262,144 keys included)
+    early = m4.FLAG_EARLY_RELEASE
 
     def step():
         for layer in range(L):

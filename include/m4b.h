@@ -95,10 +95,9 @@ enum m4b_flags {
     /* with M4B_FLAG_PDL on PHASE selector 2 and m4b_exchange_merge_wvb: release the next kernel
        of the stream as soon as this one's W_UV loads are issued, instead of at completion, so the
        next layer's weight loads overlap this merge.  The next kernel still waits for this one's
-       results.  Worth it when a layer's slab is short (measured, one-GPU layer-steps on the same
-       box: 16.9 -> 16.0 us at 4,096 keys, 23.4 -> 22.0 at 32,768, 46.0 -> 45.2 at 131,072); at
-       262,144 keys the early start competes for HBM and gains nothing.  Other entry points
-       ignore it. */
+       results.  Measured, one-GPU layer-steps on the same box: 16.9 -> 16.0 us at 4,096 keys,
+       23.4 -> 22.0 at 32,768, 46.0 -> 45.2 at 131,072, and +0.7 % layer-steps/s at 262,144 keys.
+       Other entry points ignore it. */
     M4B_FLAG_EARLY_RELEASE = 1u << 3
 };
 
