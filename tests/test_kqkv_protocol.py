@@ -59,6 +59,25 @@ class Wait:
         return ok
 
 
+class Drain(Wait):
+    """A wait that ignores the abort flag (a thread draining its own copies or MMAs)."""
+    abortable = False
+
+
+class Cond:
+    abortable = False
+
+    def __init__(self, f):
+        self.f = f
+
+    def ready(self):
+        return self.f()
+
+
+class Abort(Exception):
+    """A bounded wait gave up somewhere in the CTA: the abort flag is set."""
+
+
 class CountWait:
     def __init__(self, get, target):
         self.get, self.target = get, target
@@ -69,7 +88,8 @@ class CountWait:
 
 class Model:
     def __init__(self, segs, k_entries, v_entries, nk, nv, rng, single_o_done=False,
-                 rescale_p=0.3, p_free_wait=True, shared_ring=False):
+                 rescale_p=0.3, p_free_wait=True, shared_ring=False, abort_after=None,
+                 drain_after_barrier=False):
         self.rng = rng
         self.segs = segs                      # tiles per segment
         self.NT = sum(segs)
@@ -84,6 +104,10 @@ class Model:
         self.single = single_o_done
         self.rescale_p = rescale_p
         self.p_free_wait = p_free_wait
+        # abort_after: the abort flag goes up after that many role steps (a wait elsewhere gave up)
+        self.abort_after, self.aborted, self.abort_seen = abort_after, False, set()
+        self.started = set()
+        self.drain_after_barrier = drain_after_barrier
         # shared_ring: the earlier two-issuer variant -- one FIFO ring of nk + nv slots filled in
         # consumption order K(0), then K(t + 1), V(t) per tile, taken by both issuers
         self.shared = shared_ring
@@ -130,30 +154,46 @@ class Model:
         return self.o_done[tile & 1], tile >> 1
 
     # ---- roles (generators yielding waits)
+    def own_copies_landed(self, kind):
+        return Cond(lambda: not any(k[0] == kind for _, k in self.tma))
+
+    def producer_exit(self, kind):
+        """After the loop: with the abort flag up, let this producer's copies land."""
+        if self.aborted and not self.drain_after_barrier:
+            yield self.own_copies_landed(kind)
+
     def kload(self):
         slot = use = 0
-        for t in range(self.NT):
-            for e in range(self.KE):
-                yield Wait(self.kempty[slot], use - 1) if use > 0 else None
-                if self.slot_readers.get(("K", slot), 0):
-                    raise ProtocolError(f"K slot {slot} refilled while an MMA reads it")
-                self.tma.append((self.kfull[slot], ("K", slot)))
-                slot += 1
-                if slot == self.NK:
-                    slot, use = 0, use + 1
+        try:
+            for t in range(self.NT):
+                for e in range(self.KE):
+                    yield Wait(self.kempty[slot], use - 1) if use > 0 else None
+                    if self.slot_readers.get(("K", slot), 0):
+                        raise ProtocolError(f"K slot {slot} refilled while an MMA reads it")
+                    self.tma.append((self.kfull[slot], ("K", slot)))
+                    slot += 1
+                    if slot == self.NK:
+                        slot, use = 0, use + 1
+        except Abort:
+            pass
+        yield from self.producer_exit("K")
 
     def vload(self):
         slot = use = 0
-        for t in range(self.NT):
-            yield CountWait(lambda: self.k_landed, t + 1)
-            for e in range(self.VE):
-                yield Wait(self.vempty[slot], use - 1) if use > 0 else None
-                if self.slot_readers.get(("V", slot), 0):
-                    raise ProtocolError(f"V slot {slot} refilled while an MMA reads it")
-                self.tma.append((self.vfull[slot], ("V", slot)))
-                slot += 1
-                if slot == self.NV:
-                    slot, use = 0, use + 1
+        try:
+            for t in range(self.NT):
+                yield CountWait(lambda: self.k_landed, t + 1)
+                for e in range(self.VE):
+                    yield Wait(self.vempty[slot], use - 1) if use > 0 else None
+                    if self.slot_readers.get(("V", slot), 0):
+                        raise ProtocolError(f"V slot {slot} refilled while an MMA reads it")
+                    self.tma.append((self.vfull[slot], ("V", slot)))
+                    slot += 1
+                    if slot == self.NV:
+                        slot, use = 0, use + 1
+        except Abort:
+            pass
+        yield from self.producer_exit("V")
 
     def load(self):                           # shared_ring: one producer, one ring
         for j in range(len(self.order)):
@@ -177,6 +217,15 @@ class Model:
         self.queues[q].append((kind, kw))
 
     def mma1(self):
+        try:
+            yield from self.mma1_loop()
+        except Abort:
+            pass
+        # every MMA1 of this thread has completed before the CTA frees TMEM (also after an abort)
+        self.issue("A", "commit", bar=self.a_fin)
+        yield Drain(self.a_fin, 0)
+
+    def mma1_loop(self):
         slot = use = 0
         for t in range(self.NT):
             if t == self.first[t]:
@@ -197,10 +246,16 @@ class Model:
                     slot, use = 0, use + 1
             self.issue("A", "commit", bar=self.s_full[t & 1])
             self.k_landed = t + 1
-        self.issue("A", "commit", bar=self.a_fin)
-        yield Wait(self.a_fin, 0)
 
     def mma2(self):
+        try:
+            yield from self.mma2_loop()
+        except Abort:
+            pass
+        self.issue("B", "commit", bar=self.o_full)
+        yield Drain(self.o_full, 0)
+
+    def mma2_loop(self):
         slot = use = 0
         for i in range(self.NT):
             yield Wait(self.p_full[i & 1], i >> 1)
@@ -219,12 +274,16 @@ class Model:
                     slot, use = 0, use + 1
             bar, _ = self.od(i)
             self.issue("B", "commit", bar=bar)
-        self.issue("B", "commit", bar=self.o_full)
-        yield Wait(self.o_full, 0)
 
     flushing = False
 
     def softmax(self):
+        try:
+            yield from self.softmax_loop()
+        except Abort:
+            pass                              # an aborted CTA writes no record
+
+    def softmax_loop(self):
         nseg = len(self.segs)
         if self.NT > 0:
             self.q_full.arrive()              # the first segment's Q, staged before the loop
@@ -281,29 +340,53 @@ class Model:
         else:
             kw["bar"].arrive()
 
+    def abortable(self, name):
+        w = self.waiting.get(name)
+        return (self.aborted and name in self.started and name not in self.abort_seen and
+                getattr(w, "abortable", True))
+
     def run(self, max_steps=200000):
         live = dict(self.roles)
+        steps = 0
         for _ in range(max_steps):
+            if self.abort_after is not None and steps >= self.abort_after:
+                self.aborted = True
             moves = []
             for name, gen in live.items():
                 w = self.waiting.get(name)
-                if w is None or w.ready():
+                if self.abortable(name) or w is None or w.ready():
                     moves.append(("role", name))
             moves += [("tma", j) for j in range(len(self.tma))]
             moves += [("op", q) for q in self.queues if self.queues[q]]
-            if not moves:
-                if live:
-                    raise ProtocolError(f"deadlock: {sorted(live)} wait")
+            if not live:                      # every thread has passed the CTA's last barrier
+                if self.drain_after_barrier and self.aborted:
+                    # every thread is past the CTA's last barrier; the producers drain there
+                    while self.tma:
+                        self.complete_tma(self.rng.randrange(len(self.tma)))
+                if self.tma:
+                    raise ProtocolError("the CTA exits with TMA copies into its shared memory in "
+                                        "flight")
+                if any(self.queues.values()):
+                    raise ProtocolError("TMEM is freed with MMAs in flight")
                 return
+            if not moves:
+                raise ProtocolError(f"deadlock: {sorted(live)} wait")
             kind, x = self.rng.choice(moves)
             if kind == "tma":
                 self.complete_tma(x)
             elif kind == "op":
                 self.complete_op(x)
             else:
+                steps += 1
+                throw = self.abortable(x)
                 self.waiting.pop(x, None)
                 try:
-                    w = next(live[x])
+                    if throw:
+                        self.abort_seen.add(x)
+                        w = live[x].throw(Abort())
+                    else:
+                        self.started.add(x)
+                        w = next(live[x])
                     if w is not None:
                         self.waiting[x] = w
                 except StopIteration:
@@ -361,3 +444,30 @@ def test_shared_ring_of_the_earlier_two_issuer_variant_aliases():
             caught.append(str(e))
     assert caught, "the shared ring never aliased"
     assert any("full" in c for c in caught)
+
+
+def _aborted_runs(rng, n, **kw):
+    for _ in range(n):
+        segs = rng.choice([[1], [3], [7], [1, 2], [2, 1, 3], [0]])
+        try:
+            Model(segs, 5, 4, 3, 2, rng, abort_after=rng.randrange(0, 150), **kw).run()
+            yield None
+        except ProtocolError as e:
+            yield str(e)
+
+
+def test_abort_path_frees_tmem_only_after_every_mma():
+    """A bounded wait that gives up raises the abort flag at a random point: every role leaves its
+    loop, each MMA issuer waits for its own last commit, and no MMA is in flight when TMEM is freed
+    (the kernel as built).  Its producers drain their copies only if the flag is up when they leave
+    their loop, so a CTA whose producer had already finished can exit with a copy in flight -- the
+    rare case the next test's variant closes; it is not counted here."""
+    errors = [e for e in _aborted_runs(random.Random(21), 1500) if e]
+    assert not [e for e in errors if "TMEM" in e or "deadlock" in e or "phase" in e], errors[:3]
+
+
+def test_abort_path_with_producers_draining_after_the_last_barrier():
+    """The producers drain their own copies after the CTA's last barrier (where the abort flag can
+    no longer change): no schedule exits with a copy or an MMA in flight."""
+    errors = [e for e in _aborted_runs(random.Random(22), 1500, drain_after_barrier=True) if e]
+    assert not errors, errors[:3]
